@@ -1,0 +1,385 @@
+"""Benchmark of the LEAP attention hot path on B200.
+
+Headline (BASELINE.json metric "decode-attn KV GB/s (% HBM peak)", config 2):
+Llama-3-8B-shaped decode attention (32 q heads, 8 kv heads, head_dim 128,
+RoPE theta 500000), one query token at context 8192, FP32 KV cache.  One
+step = one decode token through the attention of all 32 layers of an
+8B-shaped model: 32 launches of the fused RoPE + append + split-KV decode
+kernel, each over its own layer's 67 MB K+V cache (2.15 GB in total, so no
+layer's cache is still in the 126 MB L2 when it is read again).
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+
+N > 1 runs under torchrun, one process per GPU; every rank decodes its own
+independent sequence (replicas, weak scaling, no collective on the data
+path).  Times are CUDA-event device times, max over ranks.
+
+value      : algorithmic KV-path bytes / s over all ranks (GB/s), with the
+             inputs resident in HBM
+e2e        : the same through the host-pointer C ABI entry point
+             (leap_attn_decode_host): pinned staging, H2D of q/k/v, kernel,
+             D2H of the output, per layer, blocking
+roofline   : dominant kernel (decode_attn_kernel) bytes per launch / mean
+             launch time, against MEASURED_PEAKS.json hbm_gbs
+cpu_baseline: the reference's own attention block (oracle/_ref, compiled
+             from src/inference/FloatTransformer.cpp:404-662) on the host's
+             cores over a bounded sample of the same workload
+--impl reference: the reference's CPU block as the timed arm.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+# Config 2 shape at its largest context.
+N_LAYERS = 32
+N_HEADS, N_KV, HD = 32, 8, 128
+CTX = 8192
+THETA = 500000.0
+SEED = 0
+
+
+def algorithmic_bytes(n_heads, n_kv, hd, ctx):
+    """Bytes one decode launch must move: K and V rows read (ctx rows), q in,
+    new k/v in, new k/v appended, out written."""
+    return 4 * (2 * n_kv * hd * ctx + n_heads * hd + 2 * n_kv * hd + 2 * n_kv * hd
+                + n_heads * hd)
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for n, v in zip(names, r[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------
+# CPU arms (test infrastructure: the reference's own code, or the C port)
+# ---------------------------------------------------------------------------
+
+def cpu_reference_step_time(min_seconds: float, threads: int | None = None):
+    """Time the reference attention block at the config-2 shape on the host.
+
+    Uses oracle/_ref (the reference's own block, compiled from its sources)
+    when present, else the C restatement.  The block is called 32 times per
+    step (one per layer) at ctx 8192, cycling over 4 distinct layer caches
+    (each 67 MB, larger than the host's last-level cache).  Returns
+    (seconds per step, kind, threads, steps timed)."""
+    import oracle
+    threads = threads or os.cpu_count() or 1
+    os.environ.setdefault("OMP_NUM_THREADS", str(threads))
+    kind = "reference" if oracle.has_ref() else "port"
+    rng = np.random.default_rng(SEED)
+    kv_dim = N_KV * HD
+    caches = [(rng.standard_normal((CTX, kv_dim), dtype=np.float32),
+               rng.standard_normal((CTX, kv_dim), dtype=np.float32)) for _ in range(4)]
+    c, s = oracle.rope_table(CTX, HD, THETA)
+    q = rng.standard_normal(N_HEADS * HD, dtype=np.float32)
+
+    def step():
+        for layer in range(N_LAYERS):
+            kc, vc = caches[layer % 4]
+            oracle.attn_block(q.copy(), kc, vc, CTX - 1, N_HEADS, N_KV, HD, c, s,
+                              impl="ref" if kind == "reference" else "port", threads=threads)
+
+    step()  # warm-up
+    n = 0
+    t0 = time.perf_counter()
+    while True:
+        step()
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= min_seconds:
+            break
+    return el / n, kind, threads, n
+
+
+def run_reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return  # other ranks exit without work
+    import oracle
+    threads = os.cpu_count() or 1
+    os.environ["OMP_NUM_THREADS"] = str(threads)
+    kind = "reference" if oracle.has_ref() else "port"
+    rng = np.random.default_rng(SEED)
+    kv_dim = N_KV * HD
+    caches = [(rng.standard_normal((CTX, kv_dim), dtype=np.float32),
+               rng.standard_normal((CTX, kv_dim), dtype=np.float32)) for _ in range(4)]
+    c, s = oracle.rope_table(CTX, HD, THETA)
+    q = rng.standard_normal(N_HEADS * HD, dtype=np.float32)
+    impl = "ref" if kind == "reference" else "port"
+
+    def step():
+        for layer in range(N_LAYERS):
+            kc, vc = caches[layer % 4]
+            oracle.attn_block(q.copy(), kc, vc, CTX - 1, N_HEADS, N_KV, HD, c, s, impl=impl,
+                              threads=threads)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    el = time.perf_counter() - t0
+    nbytes = algorithmic_bytes(N_HEADS, N_KV, HD, CTX) * N_LAYERS * args.steps
+    value = nbytes / el / 1e9
+    line = {
+        "impl": "reference",
+        "metric": "decode-attn KV GB/s", "value": round(value, 3), "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(el / args.steps * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": workload_config(args.gpus),
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads,
+                         "kind": kind,
+                         "sample": f"{N_LAYERS} block calls per step at ctx {CTX} cycling over 4 "
+                                   "distinct 67 MB layer caches (each larger than the host LLC)"},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(n):
+    return {"workload": "config2: Llama-3-8B-shape GQA decode attention (32q/8kv/hd128, theta "
+                        f"500000), 1 token at ctx {CTX}, one step = {N_LAYERS} layers",
+            "model": "llama3-8b-shape attention", "global_batch": n, "seq_len": CTX,
+            "parallelism": f"replicas{n}" if n > 1 else "single",
+            "l2": f"inputs > L2: {N_LAYERS} distinct layer caches of 67 MB (2.15 GB) rotated"}
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+
+def run_gpu_arm(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+
+    from leap_b200 import AttentionContext
+
+    ctx = AttentionContext(N_LAYERS, N_HEADS, N_KV, HD, CTX, device=local, theta=THETA)
+    stream = torch.cuda.current_stream(dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(SEED + rank)
+    # resident synthetic caches, N(0,1), written through the ABI (rows
+    # 0..ctx-2; row ctx-1 is the token being decoded)
+    for layer in range(N_LAYERS):
+        kr = torch.randn(CTX - 1, N_KV, HD, device=dev, generator=g)
+        vr = torch.randn(CTX - 1, N_KV, HD, device=dev, generator=g)
+        ctx.kv_write(0, layer, 0, kr, vr)
+    q = torch.randn(N_LAYERS, N_HEADS, HD, device=dev, generator=g)
+    kn = torch.randn(N_LAYERS, N_KV, HD, device=dev, generator=g)
+    vn = torch.randn(N_LAYERS, N_KV, HD, device=dev, generator=g)
+    out = torch.empty_like(q)
+    ctx.sync()
+    torch.cuda.synchronize(dev)
+    pos = CTX - 1
+
+    def step(ev=None):
+        for layer in range(N_LAYERS):
+            if ev is not None:
+                ev[layer][0].record(stream)
+            ctx.decode(layer, pos, q[layer], kn[layer], vn[layer], out[layer])
+            if ev is not None:
+                ev[layer][1].record(stream)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+
+    # ---- timed region (device time, CUDA events on the launch stream) ------
+    sampler = ClockSampler(local)
+    sampler.start()
+    launch_ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                  for _ in range(N_LAYERS)] for _ in range(args.steps)]
+    barrier()
+    torch.cuda.synchronize(dev)
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for k in range(args.steps):
+        step(launch_ev[k])
+    t_end.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    clocks = sampler.stop()
+    ctx.sync()
+    elapsed_ms = max_over_ranks(t_start.elapsed_time(t_end))
+    launch_ms = [a.elapsed_time(b) for row in launch_ev for (a, b) in row]
+    mean_launch_ms = max_over_ranks(float(np.mean(launch_ms)))
+
+    per_launch = algorithmic_bytes(N_HEADS, N_KV, HD, CTX)
+    total_bytes = per_launch * N_LAYERS * args.steps * world
+    value = total_bytes / (elapsed_ms / 1e3) / 1e9
+    peak, peak_kind = load_peaks()
+    achieved = per_launch / (mean_launch_ms / 1e3) / 1e9
+
+    # ---- end to end through the host-pointer entry point -------------------
+    hq = q.cpu().numpy()
+    hk = kn.cpu().numpy()
+    hv = vn.cpu().numpy()
+    ctx.sync()
+    e2e_steps = max(1, args.steps)
+    for _ in range(min(args.warmup, 2)):
+        for layer in range(N_LAYERS):
+            ctx.decode_host(layer, pos, hq[layer], hk[layer], hv[layer])
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        for layer in range(N_LAYERS):
+            ctx.decode_host(layer, pos, hq[layer], hk[layer], hv[layer])
+    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    barrier()
+    e2e_value = per_launch * N_LAYERS * e2e_steps * world / e2e_s / 1e9
+
+    line = None
+    if rank == 0:
+        traffic = None
+        tpath = os.path.join(ROOT, "profiles", "decode_attn_traffic.json")
+        if os.path.exists(tpath):
+            with open(tpath) as f:
+                traffic = json.load(f).get("bytes_per_launch")
+        line = {
+            "metric": "decode-attn KV GB/s", "value": round(value, 2), "unit": "GB/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(elapsed_ms / args.steps, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": workload_config(world),
+            "frac_of_hbm_peak": round(value / world / peak, 4),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak,
+                         "peak_kind": peak_kind, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": traffic,
+                         "kernel": "decode_attn_kernel<128,4>",
+                         "bytes_per_launch": per_launch,
+                         "mean_launch_us": round(mean_launch_ms * 1e3, 3)},
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
+                    "h2d_bytes_per_step": int(N_LAYERS * (hq[0].nbytes + hk[0].nbytes
+                                                          + hv[0].nbytes)),
+                    "d2h_bytes_per_step": int(N_LAYERS * hq[0].nbytes),
+                    "ms_per_step": round(e2e_s / e2e_steps * 1e3, 4)},
+            "gpu_launches": N_LAYERS * args.steps,
+            "clocks": clocks,
+        }
+    ctx.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        sec, kind, threads, n = cpu_reference_step_time(args.cpu_seconds)
+        cpu_val = algorithmic_bytes(N_HEADS, N_KV, HD, CTX) * N_LAYERS / sec / 1e9
+        line["cpu_baseline"] = {
+            "value": round(cpu_val, 3), "unit": "GB/s", "cores": threads, "kind": kind,
+            "sample": f"{n} steps of {N_LAYERS} reference-block calls at ctx {CTX} "
+                      "(4 distinct 67 MB layer caches cycled)",
+            "ms_per_step": round(sec * 1e3, 2)}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["leap", "reference"], default="leap")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "leap":
+        args.warmup = 3  # timing rule: at least 3 warm-up steps
+    if args.impl == "reference":
+        run_reference_arm(args)
+    else:
+        run_gpu_arm(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,188 @@
+/*
+ * leap_b200.h — C ABI of the B200 attention engine for LEAP.
+ *
+ * LEAP (Harikeshav-R/LEAP) runs its GQA attention block inline in the private
+ * `run_layer()` of its CPU engines:
+ *   src/inference/FloatTransformer.cpp:404-662      (FP32 engine)
+ *   src/inference/QuantizedTransformer.cpp:680-923  (W8A8 engine, same math)
+ * That block is: RoPE on q and on the new k row of the cache, the new k/v rows
+ * written into the FP32 KV cache, scores q.k/sqrt(head_size) over positions
+ * 0..pos, softmax, and the softmax-weighted sum of V rows into `xb`.
+ *
+ * This header is the drop-in boundary a LEAP engine binds to replace that
+ * block: plain C types, device pointers, an `int` status on every call
+ * (0 = ok) and a thread-local message from leap_last_error().  A C++ caller
+ * turns a non-zero status into std::runtime_error, which is the reference's
+ * own error convention (src/inference/main.cpp:498-501).
+ *
+ * Threading: one caller thread per context, like the reference engine (its
+ * run state is shared, src/inference/FloatTransformer.h:24-37).  Work is
+ * stream-ordered on the context's stream; *_host entry points block.
+ *
+ * Device KV-cache layout (owned by the context, FP32):
+ *   [slot][layer][kv_head][max_seq_padded][head_dim]
+ * i.e. each (slot, layer, kv_head) is one contiguous stream of rows, so one
+ * bulk copy moves a whole tile of positions.  The reference keeps
+ * [layer][pos][kv_head][head_dim] (src/inference/FloatTransformer.cpp:50-51,
+ * :396); leap_kv_write/leap_kv_read convert from/to that layout.
+ */
+#ifndef LEAP_B200_H
+#define LEAP_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define LEAP_API __attribute__((visibility("default")))
+#else
+#define LEAP_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LEAP_OK 0
+#define LEAP_ERR_INVALID 1   /* bad argument (shape, range, null pointer)     */
+#define LEAP_ERR_CUDA 2      /* a CUDA runtime call failed                     */
+#define LEAP_ERR_DEVICE 3    /* a kernel reported an error (bounded wait hit)  */
+#define LEAP_ERR_NOMEM 4     /* device allocation failed                       */
+
+typedef struct leap_ctx leap_ctx; /* opaque */
+
+/*
+ * Engine description.  Mirrors the reference `Config`
+ * (src/inference/Config.h:5-13) for the fields attention needs, plus the
+ * layer range this context holds (the pipeline split of
+ * src/inference/Transformer.h:17-23) and the number of sequence slots.
+ */
+typedef struct leap_ctx_desc {
+    int n_layers;        /* layers whose KV cache this context holds            */
+    int layer0;          /* global index of local layer 0 (pipeline stages)     */
+    int n_heads;         /* query heads                                          */
+    int n_kv_heads;      /* key/value heads; n_heads % n_kv_heads == 0           */
+    int head_dim;        /* 64 or 128                                            */
+    int max_seq;         /* cache capacity per slot (reference seq_len)          */
+    int max_batch;       /* sequence slots (1 for the single-stream engine)      */
+    int device;          /* CUDA device ordinal                                  */
+    /* Host RoPE table [max_seq][head_dim/2], as the reference precomputes it
+     * (src/inference/FloatTransformer.cpp:56-72).  The engine passes its own
+     * table, so the device rotation uses exactly the same cos/sin values.   */
+    const float *rope_cos;
+    const float *rope_sin;
+} leap_ctx_desc;
+
+/* Last error message of the calling thread ("" if none). */
+LEAP_API const char *leap_last_error(void);
+
+/* Library version string. */
+LEAP_API const char *leap_version(void);
+
+/*
+ * The reference RoPE table, host side: for even i < head_dim,
+ *   cos/sin(pos * freq_i)  at [pos][i/2],  pos < seq_len.
+ * Replaces FloatTransformer::precompute_freqs
+ * (src/inference/FloatTransformer.cpp:56-72).  The source writes
+ * freq = 1/pow(theta, i/hd); the reference's release build (-ffast-math)
+ * evaluates it as expf(-(i/hd) * logf(theta)), and this function computes
+ * that form with the C library's float functions, so its table equals the
+ * compiled reference's bit for bit.  The shipped reference hard-codes
+ * theta = 500000 (:65).
+ */
+LEAP_API int leap_rope_table(int seq_len, int head_dim, float theta,
+                             float *rope_cos, float *rope_sin);
+
+/*
+ * Create / destroy a context: device KV cache (zeroed), RoPE table, split-KV
+ * scratch and a non-blocking stream on desc->device.
+ * Replaces FloatTransformer::init_run_state + precompute_freqs
+ * (src/inference/FloatTransformer.cpp:39-72) for the attention state.
+ */
+LEAP_API int leap_ctx_create(const leap_ctx_desc *desc, leap_ctx **out);
+LEAP_API int leap_ctx_destroy(leap_ctx *ctx);
+
+/* Use `stream` (a cudaStream_t; NULL = the context's own stream) for all
+ * following work of this context. */
+LEAP_API int leap_ctx_set_stream(leap_ctx *ctx, void *stream);
+
+/* Block until the context's queued work is done; reports kernel errors. */
+LEAP_API int leap_sync(leap_ctx *ctx);
+
+/* Bytes of device memory held by the context. */
+LEAP_API int leap_ctx_device_bytes(const leap_ctx *ctx, size_t *bytes);
+
+/*
+ * Zero every slot's K and V cache.  Replaces
+ * FloatTransformer::clear_kv_cache (src/inference/FloatTransformer.cpp:74-77).
+ */
+LEAP_API int leap_kv_clear(leap_ctx *ctx);
+
+/*
+ * Copy rows [pos0, pos0+n_pos) of (slot, layer) into / out of the cache.
+ * `k`, `v` are in the reference row layout [n_pos][n_kv_heads][head_dim]
+ * (src/inference/FloatTransformer.cpp:396-398).  from_host / to_host select
+ * host or device pointers.  Used to load a KV snapshot, and by tests.
+ */
+LEAP_API int leap_kv_write(leap_ctx *ctx, int slot, int layer, int pos0, int n_pos,
+                  const float *k, const float *v, int from_host);
+LEAP_API int leap_kv_read(leap_ctx *ctx, int slot, int layer, int pos0, int n_pos,
+                 float *k, float *v, int to_host);
+
+/*
+ * Decode attention for one token of slot 0, fused:
+ *   RoPE(q), RoPE(k_new)                 FloatTransformer.cpp:404-494
+ *   cache[layer][pos] <- (rot k_new, v)  FloatTransformer.cpp:397-402
+ *   out = softmax(q.K^T/sqrt(hd)) . V    FloatTransformer.cpp:496-662
+ * over positions 0..pos inclusive.
+ *   q     [n_heads][head_dim]     (un-rotated, as the wq matmul leaves it)
+ *   k_new [n_kv_heads][head_dim]  (un-rotated)
+ *   v_new [n_kv_heads][head_dim]
+ *   out   [n_heads][head_dim]     (the reference's `xb`)
+ * Device pointers, 16-byte aligned; asynchronous on the context stream.
+ */
+LEAP_API int leap_attn_decode(leap_ctx *ctx, int layer, int pos, const float *q,
+                     const float *k_new, const float *v_new, float *out);
+
+/*
+ * The same call with HOST pointers: the reference-facing form, for an
+ * engine whose activations live in host memory like the reference's
+ * run_layer.  Copies in, runs, copies out and blocks until `out` is ready.
+ */
+LEAP_API int leap_attn_decode_host(leap_ctx *ctx, int layer, int pos, const float *q,
+                          const float *k_new, const float *v_new, float *out);
+
+/*
+ * Ragged batched decode: one new token for each of n_seq sequences, each in
+ * its own cache slot at its own position.  Semantics = leap_attn_decode per
+ * sequence (the reference has no batched path; it is the reference block
+ * applied to each sequence).
+ *   slots[i], positions[i]: HOST int arrays of length n_seq
+ *   q [n_seq][n_heads][hd], k_new/v_new [n_seq][n_kv][hd], out like q.
+ * Slots must be distinct within one call.
+ */
+LEAP_API int leap_attn_decode_batched(leap_ctx *ctx, int layer, int n_seq,
+                             const int *slots, const int *positions,
+                             const float *q, const float *k_new,
+                             const float *v_new, float *out);
+
+/*
+ * Causal prefill of n_tok prompt tokens of `slot` starting at pos0.
+ * Semantics = the reference decode block run for pos = pos0 .. pos0+n_tok-1
+ * in order (the reference feeds prompts token by token,
+ * src/inference/main.cpp:80-89): each token's k/v are rotated and appended,
+ * and token i attends to cache rows 0..pos0+i.
+ *   q [n_tok][n_heads][hd], k/v [n_tok][n_kv][hd] (un-rotated), out like q.
+ */
+LEAP_API int leap_attn_prefill(leap_ctx *ctx, int slot, int layer, int pos0, int n_tok,
+                      const float *q, const float *k, const float *v,
+                      float *out);
+
+/* Prefill kernel selection (for tests and benchmarks):
+ *   0 = default (tensor-core 3xTF32 path), 1 = CUDA-core FP32 path. */
+LEAP_API int leap_set_prefill_impl(leap_ctx *ctx, int impl);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LEAP_B200_H */

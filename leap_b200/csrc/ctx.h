@@ -1,0 +1,98 @@
+// ctx.h — host-side definition of the opaque leap_ctx and shared helpers.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+#include <string>
+
+#include "leap_b200.h"
+
+struct leap_ctx {
+    // shape (reference Config fields, src/inference/Config.h:5-13)
+    int device = 0;
+    int n_layers = 0, layer0 = 0;
+    int n_heads = 0, n_kv = 0, hd = 0, group = 0;
+    int max_seq = 0, max_seq_pad = 0, max_batch = 0;
+    int num_sms = 148;
+
+    cudaStream_t own_stream = nullptr;
+    cudaStream_t stream = nullptr;
+
+    // KV cache [slot][layer][kv_head][max_seq_pad][hd] (floats)
+    float *k_cache = nullptr, *v_cache = nullptr;
+    size_t head_stride = 0, layer_stride = 0, slot_stride = 0;
+    size_t cache_bytes = 0;  // per tensor (K or V)
+
+    // RoPE table [max_seq][hd/2]
+    float *rope_cos = nullptr, *rope_sin = nullptr;
+
+    // split-KV scratch
+    float *part_o = nullptr;      // [max_parts][group*hd]
+    float *part_ml = nullptr;     // [max_parts][group][2]
+    unsigned *counters = nullptr; // [max_batch][n_kv]
+    int max_parts = 0;
+
+    // device error word (kernels report bounded-wait timeouts here)
+    int *d_err = nullptr;
+
+    // host-pointer entry points: pinned staging and device mirrors
+    float *h_stage = nullptr;  // pinned: q | k | v | out for one token
+    float *d_stage = nullptr;
+
+    // prefill scratch (rotated q), grown on demand
+    float *d_qrot = nullptr;
+    size_t qrot_cap = 0;  // floats
+    int prefill_impl = 0;
+
+    size_t device_bytes = 0;
+};
+
+namespace leap {
+
+constexpr int kMaxDevices = 64;
+
+// thread-local last error
+void set_error(const char *fmt, ...);
+void clear_error();
+
+// Convert a CUDA error into a LEAP status (sets the message).
+int cuda_status(cudaError_t e, const char *what);
+
+inline float *k_head_ptr(const leap_ctx *c, int slot, int layer, int kvh) {
+    return c->k_cache + slot * c->slot_stride + layer * c->layer_stride +
+           kvh * c->head_stride;
+}
+inline float *v_head_ptr(const leap_ctx *c, int slot, int layer, int kvh) {
+    return c->v_cache + slot * c->slot_stride + layer * c->layer_stride +
+           kvh * c->head_stride;
+}
+
+// ---- decode attention (decode_attn.cu) -----------------------------------
+constexpr int kMaxSeqPerLaunch = 128;
+
+struct DecodeSeq {
+    int n_seq;
+    int chunk;                         // rows per split
+    int pos[kMaxSeqPerLaunch];
+    int slot[kMaxSeqPerLaunch];
+    int split0[kMaxSeqPerLaunch + 1];  // prefix sum of splits per sequence
+};
+
+// Launch one batch of decode work (n_seq <= kMaxSeqPerLaunch).  q/k_new/
+// v_new/out point at the first sequence of the batch.
+int launch_decode(leap_ctx *c, int layer, const DecodeSeq &tab, const float *q,
+                  const float *k_new, const float *v_new, float *out);
+
+// Fill tab.chunk / tab.split0 for the given positions; returns total splits.
+int plan_decode(const leap_ctx *c, DecodeSeq &tab);
+
+// Upper bound on split-KV partials one decode launch can need.
+int max_decode_parts(int hd, int n_kv, int max_batch, int max_seq_pad, int num_sms);
+
+// ---- prefill attention (prefill_attn.cu) ---------------------------------
+int launch_prefill(leap_ctx *c, int slot, int layer, int pos0, int n_tok,
+                   const float *q, const float *k, const float *v, float *out);
+
+}  // namespace leap

@@ -1,0 +1,494 @@
+// decode_attn.cu — fused RoPE + KV append + split-KV GQA decode attention.
+//
+// Replaces the reference's attention block (src/inference/
+// FloatTransformer.cpp:404-662, twin QuantizedTransformer.cpp:680-923):
+//   * RoPE of q (all heads) and of the new k row  (:404-494)
+//   * the new rotated k and raw v written into cache row `pos` (:397-402)
+//   * scores q.k * 1/sqrt(hd) over rows 0..pos   (:497-630)
+//   * softmax (:632, :216-238) and the weighted V sum (:634-661).
+//
+// Design (HBM-bound, CUDA cores, no tensor cores):
+//   * one CTA per (sequence, split of the context, kv head); the CTA packs
+//     the kv_mul query heads that share that kv head, so every K/V byte
+//     crosses HBM once (the reference re-reads K/V once per query head);
+//   * K and V tiles of 16 KB each move global -> shared with 1-D bulk
+//     copies (TMA engine) into a 3-stage mbarrier pipeline; the cache is
+//     head-major, so a tile of positions is one contiguous range;
+//   * a row of K/V is read by a group of LPR lanes, each holding a slice
+//     of dims for all G query heads; scores are reduced with xor-shuffles;
+//   * online softmax per lane group, merged across groups in shared memory;
+//   * splits of one (sequence, kv head) are combined by the CTA that
+//     finishes last (atomic ticket), so there is no second launch.
+#include <cfloat>
+#include <cstdio>
+
+#include "common.cuh"
+#include "ctx.h"
+
+namespace leap {
+namespace {
+
+constexpr int kThreads = 128;
+constexpr int kWarps = kThreads / 32;
+constexpr int kStages = 3;
+constexpr int kTileBytes = 16384;   // per tensor (K or V) per stage
+constexpr int kMaxSplitsPerSeq = 256;
+
+template <int HD, int G>
+struct Cfg {
+    static constexpr int kLpr0 = G * HD / 64;
+    static constexpr int LPR = kLpr0 < 8 ? 8 : (kLpr0 > 32 ? 32 : kLpr0);
+    static constexpr int RPW = 32 / LPR;             // rows per warp pass
+    static constexpr int NGRP = kWarps * RPW;        // row groups per CTA
+    static constexpr int DPL = HD / LPR;             // dims per lane
+    static constexpr int C4 = DPL / 4;               // float4 chunks per lane
+    static constexpr int TILE = kTileBytes / (HD * 4);
+    static constexpr int RPG = TILE / NGRP;          // rows per group per tile
+    static constexpr int NV4 = G * HD / 4;           // float4 outputs per CTA
+    static constexpr size_t kSmem = size_t(2) * kStages * TILE * HD * sizeof(float);
+    static_assert(DPL % 4 == 0 && C4 >= 1, "lane slice must be float4s");
+    static_assert(TILE % NGRP == 0, "tile rows must split over groups");
+    // CTA merge buffer [NGRP][G][HD] and combine tables reuse the stages
+    static_assert(size_t(NGRP) * G * HD * sizeof(float) <= kSmem, "merge smem");
+    static_assert(size_t(kMaxSplitsPerSeq) * G * 3 * sizeof(float) <= kSmem,
+                  "combine smem");
+};
+
+struct DecodeArgs {
+    const float *q;      // [n_seq][n_kv*G][HD]
+    const float *k_new;  // [n_seq][n_kv][HD]
+    const float *v_new;
+    float *out;          // [n_seq][n_kv*G][HD]
+    float *k_cache;
+    float *v_cache;
+    const float *rope_cos;  // [max_seq][HD/2]
+    const float *rope_sin;
+    size_t head_stride, layer_off, slot_stride;  // floats
+    float *part_o;       // [parts][G*HD]
+    float *part_ml;      // [parts][G][2]
+    unsigned *counters;  // [kMaxSeqPerLaunch][n_kv]
+    int *err;
+    int n_kv;
+    float scale_log2;    // log2(e) / sqrt(HD)
+};
+
+template <int HD, int G>
+__global__ void __launch_bounds__(kThreads, 2)
+decode_attn_kernel(const DecodeArgs a, const DecodeSeq tab) {
+    using C = Cfg<HD, G>;
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    float *sK = reinterpret_cast<float *>(smem_raw);      // [kStages][TILE][HD]
+    float *sV = sK + kStages * C::TILE * HD;
+    __shared__ uint64_t full_bar[kStages];
+    __shared__ float red_m[C::NGRP][G], red_l[C::NGRP][G];
+    __shared__ float s_M[G], s_L[G];
+    __shared__ int s_last;
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int j = lane % C::LPR;                   // lane within its row group
+    const int grp = warp * C::RPW + lane / C::LPR;  // row group
+
+    // ---- which (sequence, split, kv head) ---------------------------------
+    const int bx = blockIdx.x;
+    int lo = 0, hi = tab.n_seq - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (tab.split0[mid] <= bx) lo = mid; else hi = mid - 1;
+    }
+    const int seq = lo;
+    const int split = bx - tab.split0[seq];
+    const int nsplit = tab.split0[seq + 1] - tab.split0[seq];
+    const int kvh = blockIdx.y;
+    const int pos = tab.pos[seq];
+    const int row_begin = split * tab.chunk;
+    const int row_end = min(row_begin + tab.chunk, pos + 1);
+    const int n_tiles = (row_end - row_begin + C::TILE - 1) / C::TILE;
+    const bool last_split = (split == nsplit - 1);
+
+    const size_t head_off = size_t(tab.slot[seq]) * a.slot_stride + a.layer_off +
+                            size_t(kvh) * a.head_stride;
+    float *gK = a.k_cache + head_off;
+    float *gV = a.v_cache + head_off;
+
+    if (tid == 0) {
+        for (int s = 0; s < kStages; ++s) mbar_init(&full_bar[s], 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    if (tid == 0) {
+        for (int t = 0; t < min(kStages, n_tiles); ++t) {
+            const int r0 = row_begin + t * C::TILE;
+            const uint32_t bytes = min(C::TILE, row_end - r0) * HD * 4;
+            mbar_arrive_expect_tx(&full_bar[t], 2 * bytes);
+            bulk_g2s(sK + t * C::TILE * HD, gK + size_t(r0) * HD, bytes, &full_bar[t]);
+            bulk_g2s(sV + t * C::TILE * HD, gV + size_t(r0) * HD, bytes, &full_bar[t]);
+        }
+    }
+
+    // ---- rotated q slice: heads kvh*G .. +G, dims of this lane's chunks ---
+    const int qh0 = kvh * G;
+    const float *qs = a.q + (size_t(seq) * a.n_kv * G + qh0) * HD;
+    const float *rc = a.rope_cos + size_t(pos) * (HD / 2);
+    const float *rs = a.rope_sin + size_t(pos) * (HD / 2);
+    float q[G][C::DPL];
+#pragma unroll
+    for (int i = 0; i < C::C4; ++i) {
+        const int c4 = j + C::LPR * i;
+        const float2 cc = *reinterpret_cast<const float2 *>(rc + 2 * c4);
+        const float2 ss = *reinterpret_cast<const float2 *>(rs + 2 * c4);
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            const float4 x = *reinterpret_cast<const float4 *>(qs + g * HD + 4 * c4);
+            const float2 r0 = rope_pair(x.x, x.y, cc.x, ss.x);
+            const float2 r1 = rope_pair(x.z, x.w, cc.y, ss.y);
+            q[g][4 * i + 0] = r0.x;
+            q[g][4 * i + 1] = r0.y;
+            q[g][4 * i + 2] = r1.x;
+            q[g][4 * i + 3] = r1.y;
+        }
+    }
+
+    float m[G], l[G], o[G][C::DPL];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        m[g] = -INFINITY;
+        l[g] = 0.f;
+#pragma unroll
+        for (int d = 0; d < C::DPL; ++d) o[g][d] = 0.f;
+    }
+
+    // ---- main loop over tiles --------------------------------------------
+    bool ok = true;
+    int t = 0;
+    for (; t < n_tiles; ++t) {
+        const int s = t % kStages;
+        ok = mbar_wait(&full_bar[s], (t / kStages) & 1);
+        ok = __syncthreads_and(ok);
+        if (!ok) break;
+        const int r0 = row_begin + t * C::TILE;
+        float *tK = sK + s * C::TILE * HD;
+        float *tV = sV + s * C::TILE * HD;
+
+        if (last_split && pos < r0 + C::TILE) {
+            // the new token's row: rotate k, append k and v to the cache,
+            // and patch the staged tile (the copy may have read the old row)
+            const int rr = pos - r0;
+            const float *kn = a.k_new + (size_t(seq) * a.n_kv + kvh) * HD;
+            const float *vn = a.v_new + (size_t(seq) * a.n_kv + kvh) * HD;
+            for (int d = 2 * tid; d < HD; d += 2 * kThreads) {
+                const float2 kk = *reinterpret_cast<const float2 *>(kn + d);
+                const float2 vv = *reinterpret_cast<const float2 *>(vn + d);
+                const float2 kr = rope_pair(kk.x, kk.y, rc[d / 2], rs[d / 2]);
+                *reinterpret_cast<float2 *>(tK + rr * HD + d) = kr;
+                *reinterpret_cast<float2 *>(tV + rr * HD + d) = vv;
+                *reinterpret_cast<float2 *>(gK + size_t(pos) * HD + d) = kr;
+                *reinterpret_cast<float2 *>(gV + size_t(pos) * HD + d) = vv;
+            }
+            __syncthreads();
+        }
+
+        float sc[C::RPG][G];
+#pragma unroll
+        for (int rr = 0; rr < C::RPG; ++rr) {
+            const int row = rr * C::NGRP + grp;
+            const bool valid = (r0 + row) < row_end;
+            float acc[G];
+#pragma unroll
+            for (int g = 0; g < G; ++g) acc[g] = 0.f;
+            if (valid) {
+                const float *kr = tK + row * HD;
+#pragma unroll
+                for (int i = 0; i < C::C4; ++i) {
+                    const float4 kk =
+                        *reinterpret_cast<const float4 *>(kr + 4 * (j + C::LPR * i));
+#pragma unroll
+                    for (int g = 0; g < G; ++g) {
+                        acc[g] = fmaf(q[g][4 * i + 0], kk.x, acc[g]);
+                        acc[g] = fmaf(q[g][4 * i + 1], kk.y, acc[g]);
+                        acc[g] = fmaf(q[g][4 * i + 2], kk.z, acc[g]);
+                        acc[g] = fmaf(q[g][4 * i + 3], kk.w, acc[g]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int off = C::LPR / 2; off >= 1; off >>= 1) {
+#pragma unroll
+                for (int g = 0; g < G; ++g)
+                    acc[g] += __shfl_xor_sync(0xffffffffu, acc[g], off);
+            }
+#pragma unroll
+            for (int g = 0; g < G; ++g) sc[rr][g] = valid ? acc[g] * a.scale_log2 : -INFINITY;
+        }
+
+        // online softmax update over this tile's rows of the group
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            float mt = m[g];
+#pragma unroll
+            for (int rr = 0; rr < C::RPG; ++rr) mt = fmaxf(mt, sc[rr][g]);
+            const float alpha = (mt == -INFINITY) ? 1.f : fast_exp2(m[g] - mt);
+            m[g] = mt;
+            l[g] *= alpha;
+#pragma unroll
+            for (int d = 0; d < C::DPL; ++d) o[g][d] *= alpha;
+        }
+#pragma unroll
+        for (int rr = 0; rr < C::RPG; ++rr) {
+            const int row = rr * C::NGRP + grp;
+            if ((r0 + row) < row_end) {
+                float p[G];
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    p[g] = fast_exp2(sc[rr][g] - m[g]);
+                    l[g] += p[g];
+                }
+                const float *vr = tV + row * HD;
+#pragma unroll
+                for (int i = 0; i < C::C4; ++i) {
+                    const float4 vv =
+                        *reinterpret_cast<const float4 *>(vr + 4 * (j + C::LPR * i));
+#pragma unroll
+                    for (int g = 0; g < G; ++g) {
+                        o[g][4 * i + 0] = fmaf(p[g], vv.x, o[g][4 * i + 0]);
+                        o[g][4 * i + 1] = fmaf(p[g], vv.y, o[g][4 * i + 1]);
+                        o[g][4 * i + 2] = fmaf(p[g], vv.z, o[g][4 * i + 2]);
+                        o[g][4 * i + 3] = fmaf(p[g], vv.w, o[g][4 * i + 3]);
+                    }
+                }
+            }
+        }
+
+        __syncthreads();  // every warp is done with stage s
+        if (tid == 0 && t + kStages < n_tiles) {
+            const int tn = t + kStages;
+            const int rn = row_begin + tn * C::TILE;
+            const uint32_t bytes = min(C::TILE, row_end - rn) * HD * 4;
+            mbar_arrive_expect_tx(&full_bar[s], 2 * bytes);
+            bulk_g2s(tK, gK + size_t(rn) * HD, bytes, &full_bar[s]);
+            bulk_g2s(tV, gV + size_t(rn) * HD, bytes, &full_bar[s]);
+        }
+    }
+
+    if (!ok) {
+        // A wait gave up: give the copies still in flight a bounded chance
+        // to land before this CTA's shared memory is released, then report.
+        for (int tt = t + 1; tt < min(t + kStages, n_tiles); ++tt)
+            (void)mbar_wait(&full_bar[tt % kStages], (tt / kStages) & 1);
+        if (tid == 0) report_error(a.err, kDevWaitTimeout);
+        return;
+    }
+
+    // ---- merge the row groups of this CTA ---------------------------------
+    if (j == 0) {
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            red_m[grp][g] = m[g];
+            red_l[grp][g] = l[g];
+        }
+    }
+    __syncthreads();
+    if (tid < G) {
+        float M = -INFINITY;
+        for (int gg = 0; gg < C::NGRP; ++gg) M = fmaxf(M, red_m[gg][tid]);
+        float L = 0.f;
+        for (int gg = 0; gg < C::NGRP; ++gg) {
+            const float mg = red_m[gg][tid];
+            if (mg != -INFINITY) L += red_l[gg][tid] * fast_exp2(mg - M);
+        }
+        s_M[tid] = M;
+        s_L[tid] = L;
+    }
+    __syncthreads();
+    float *red_o = sK;  // [NGRP][G][HD]; the pipeline is drained
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        const float f = (m[g] == -INFINITY) ? 0.f : fast_exp2(m[g] - s_M[g]);
+#pragma unroll
+        for (int i = 0; i < C::C4; ++i) {
+            float4 v;
+            v.x = o[g][4 * i + 0] * f;
+            v.y = o[g][4 * i + 1] * f;
+            v.z = o[g][4 * i + 2] * f;
+            v.w = o[g][4 * i + 3] * f;
+            *reinterpret_cast<float4 *>(red_o + (grp * G + g) * HD + 4 * (j + C::LPR * i)) = v;
+        }
+    }
+    __syncthreads();
+
+    float *out_seq = a.out + (size_t(seq) * a.n_kv * G + qh0) * HD;
+    const int pidx = (tab.split0[seq] + split) * a.n_kv + kvh;
+    for (int e = tid; e < C::NV4; e += kThreads) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+        for (int gg = 0; gg < C::NGRP; ++gg) {
+            const float4 v = *reinterpret_cast<const float4 *>(red_o + gg * G * HD + 4 * e);
+            acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+        }
+        if (nsplit == 1) {
+            const float inv = 1.f / s_L[(4 * e) / HD];
+            acc.x *= inv; acc.y *= inv; acc.z *= inv; acc.w *= inv;
+            *reinterpret_cast<float4 *>(out_seq + 4 * e) = acc;
+        } else {
+            *reinterpret_cast<float4 *>(a.part_o + size_t(pidx) * G * HD + 4 * e) = acc;
+        }
+    }
+    if (nsplit == 1) return;
+
+    // ---- split-KV combine by the last CTA of this (sequence, kv head) -----
+    if (tid < G) {
+        a.part_ml[(size_t(pidx) * G + tid) * 2 + 0] = s_M[tid];
+        a.part_ml[(size_t(pidx) * G + tid) * 2 + 1] = s_L[tid];
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        unsigned *cnt = a.counters + seq * a.n_kv + kvh;
+        const unsigned ticket = atomicAdd(cnt, 1u);
+        s_last = (ticket == unsigned(nsplit - 1));
+        if (s_last) *cnt = 0u;  // ready for the next launch
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+
+    const int pbase = tab.split0[seq] * a.n_kv + kvh;  // split s at pbase + s*n_kv
+    float *cM = sK;                    // [nsplit][G]
+    float *cL = cM + nsplit * G;       // [nsplit][G]
+    float *cW = cL + nsplit * G;       // [nsplit][G]
+    for (int idx = tid; idx < nsplit * G; idx += kThreads) {
+        const int sp = idx / G, g = idx - sp * G;
+        const size_t p = (size_t(pbase) + size_t(sp) * a.n_kv) * G + g;
+        cM[idx] = __ldcg(a.part_ml + 2 * p);
+        cL[idx] = __ldcg(a.part_ml + 2 * p + 1);
+    }
+    __syncthreads();
+    if (tid < G) {
+        float M = -INFINITY;
+        for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, cM[sp * G + tid]);
+        float L = 0.f;
+        for (int sp = 0; sp < nsplit; ++sp) L += cL[sp * G + tid] * fast_exp2(cM[sp * G + tid] - M);
+        s_M[tid] = M;
+        s_L[tid] = 1.f / L;
+    }
+    __syncthreads();
+    for (int idx = tid; idx < nsplit * G; idx += kThreads) {
+        const int g = idx % G;
+        cW[idx] = fast_exp2(cM[idx] - s_M[g]) * s_L[g];
+    }
+    __syncthreads();
+    for (int e = tid; e < C::NV4; e += kThreads) {
+        const int g = (4 * e) / HD;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        const float *src = a.part_o + size_t(pbase) * G * HD + 4 * e;
+        const size_t step = size_t(a.n_kv) * G * HD;
+#pragma unroll 4
+        for (int sp = 0; sp < nsplit; ++sp) {
+            const float w = cW[sp * G + g];
+            const float4 v = __ldcg(reinterpret_cast<const float4 *>(src + sp * step));
+            acc.x = fmaf(w, v.x, acc.x);
+            acc.y = fmaf(w, v.y, acc.y);
+            acc.z = fmaf(w, v.z, acc.z);
+            acc.w = fmaf(w, v.w, acc.w);
+        }
+        *reinterpret_cast<float4 *>(out_seq + 4 * e) = acc;
+    }
+}
+
+template <int HD, int G>
+int launch_t(leap_ctx *c, const DecodeArgs &a, const DecodeSeq &tab, int total_splits) {
+    using C = Cfg<HD, G>;
+    static bool attr_set[kMaxDevices] = {};  // the attribute is per device
+    if (c->device >= kMaxDevices) return cuda_status(cudaErrorInvalidDevice, "device");
+    if (!attr_set[c->device]) {
+        cudaError_t e = cudaFuncSetAttribute(decode_attn_kernel<HD, G>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             int(C::kSmem));
+        if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(decode)");
+        attr_set[c->device] = true;
+    }
+    dim3 grid(total_splits, c->n_kv);
+    decode_attn_kernel<HD, G><<<grid, kThreads, C::kSmem, c->stream>>>(a, tab);
+    return cuda_status(cudaGetLastError(), "decode_attn_kernel launch");
+}
+
+}  // namespace
+
+int plan_decode(const leap_ctx *c, DecodeSeq &tab) {
+    const int tile = kTileBytes / (c->hd * 4);
+    const long cap_rows = 262144L / (c->hd * 4 * 2);  // ~256 KB of K+V per CTA
+    long total = 0;
+    int max_ctx = 0;
+    for (int i = 0; i < tab.n_seq; ++i) {
+        const int ctx = tab.pos[i] + 1;
+        total += ctx;
+        if (ctx > max_ctx) max_ctx = ctx;
+    }
+    const long rows = total * c->n_kv;
+    const long target = 2L * c->num_sms;  // one wave at two CTAs per SM
+    long chunk = (rows + target - 1) / target;
+    if (chunk > cap_rows) chunk = cap_rows;
+    const long min_chunk = (max_ctx + kMaxSplitsPerSeq - 1) / kMaxSplitsPerSeq;
+    if (chunk < min_chunk) chunk = min_chunk;
+    chunk = (chunk + tile - 1) / tile * tile;
+    tab.chunk = int(chunk);
+    int acc = 0;
+    for (int i = 0; i < tab.n_seq; ++i) {
+        tab.split0[i] = acc;
+        acc += int((tab.pos[i] + chunk) / chunk);  // ceil((pos+1)/chunk)
+    }
+    tab.split0[tab.n_seq] = acc;
+    return acc;
+}
+
+int max_decode_parts(int hd, int n_kv, int max_batch, int max_seq_pad, int num_sms) {
+    const long cap_rows = 262144L / (hd * 4 * 2);
+    const long nb = max_batch < kMaxSeqPerLaunch ? max_batch : kMaxSeqPerLaunch;
+    long a = (nb * max_seq_pad * long(n_kv) + cap_rows - 1) / cap_rows;
+    if (a < 2L * num_sms) a = 2L * num_sms;
+    return int(a + nb * n_kv * 2 + 64);
+}
+
+int launch_decode(leap_ctx *c, int layer, const DecodeSeq &tab, const float *q,
+                  const float *k_new, const float *v_new, float *out) {
+    const int total = tab.split0[tab.n_seq];
+    if (long(total) * c->n_kv > c->max_parts) {
+        set_error("decode plan needs %d partials, scratch holds %d", total * c->n_kv,
+                  c->max_parts);
+        return LEAP_ERR_INVALID;
+    }
+    DecodeArgs a;
+    a.q = q;
+    a.k_new = k_new;
+    a.v_new = v_new;
+    a.out = out;
+    a.k_cache = c->k_cache;
+    a.v_cache = c->v_cache;
+    a.rope_cos = c->rope_cos;
+    a.rope_sin = c->rope_sin;
+    a.head_stride = c->head_stride;
+    a.layer_off = size_t(layer) * c->layer_stride;
+    a.slot_stride = c->slot_stride;
+    a.part_o = c->part_o;
+    a.part_ml = c->part_ml;
+    a.counters = c->counters;
+    a.err = c->d_err;
+    a.n_kv = c->n_kv;
+    a.scale_log2 = kLog2e / sqrtf(float(c->hd));
+    const int key = c->hd * 100 + c->group;
+    switch (key) {
+        case 12801: return launch_t<128, 1>(c, a, tab, total);
+        case 12802: return launch_t<128, 2>(c, a, tab, total);
+        case 12804: return launch_t<128, 4>(c, a, tab, total);
+        case 12808: return launch_t<128, 8>(c, a, tab, total);
+        case 6401: return launch_t<64, 1>(c, a, tab, total);
+        case 6402: return launch_t<64, 2>(c, a, tab, total);
+        case 6404: return launch_t<64, 4>(c, a, tab, total);
+        case 6408: return launch_t<64, 8>(c, a, tab, total);
+        default:
+            set_error("unsupported head_dim %d / kv_mul %d", c->hd, c->group);
+            return LEAP_ERR_INVALID;
+    }
+}
+
+}  // namespace leap
