@@ -206,12 +206,14 @@ def run_reference_arm(args):
     print(json.dumps(line), flush=True)
 
 
-def workload_config(n):
+def workload_config(n, n_layers=N_LAYERS, ctx=CTX):
+    mb = algorithmic_bytes(N_HEADS, N_KV, HD, ctx) / 1e6
     return {"workload": "config2: Llama-3-8B-shape GQA decode attention (32q/8kv/hd128, theta "
-                        f"500000), 1 token at ctx {CTX}, one step = {N_LAYERS} layers",
-            "model": "llama3-8b-shape attention", "global_batch": n, "seq_len": CTX,
+                        f"500000), 1 token at ctx {ctx}, one step = {n_layers} layers",
+            "model": "llama3-8b-shape attention", "global_batch": n, "seq_len": ctx,
             "parallelism": f"replicas{n}" if n > 1 else "single",
-            "l2": f"inputs > L2: {N_LAYERS} distinct layer caches of 67 MB (2.15 GB) rotated"}
+            "l2": f"inputs > L2: {n_layers} distinct layer caches of {mb:.0f} MB "
+                  f"({n_layers * mb / 1e3:.2f} GB) rotated"}
 
 
 # ---------------------------------------------------------------------------
@@ -234,31 +236,29 @@ def run_gpu_arm(args):
 
     from leap_b200 import AttentionContext
 
-    ctx = AttentionContext(N_LAYERS, N_HEADS, N_KV, HD, CTX, device=local, theta=THETA)
+    n_layers, ctx_len = args.layers, args.ctx
+    ctx = AttentionContext(n_layers, N_HEADS, N_KV, HD, ctx_len, device=local, theta=THETA)
     stream = torch.cuda.current_stream(dev)
     g = torch.Generator(device=dev)
     g.manual_seed(SEED + rank)
     # resident synthetic caches, N(0,1), written through the ABI (rows
     # 0..ctx-2; row ctx-1 is the token being decoded)
-    for layer in range(N_LAYERS):
-        kr = torch.randn(CTX - 1, N_KV, HD, device=dev, generator=g)
-        vr = torch.randn(CTX - 1, N_KV, HD, device=dev, generator=g)
+    for layer in range(n_layers):
+        kr = torch.randn(ctx_len - 1, N_KV, HD, device=dev, generator=g)
+        vr = torch.randn(ctx_len - 1, N_KV, HD, device=dev, generator=g)
         ctx.kv_write(0, layer, 0, kr, vr)
-    q = torch.randn(N_LAYERS, N_HEADS, HD, device=dev, generator=g)
-    kn = torch.randn(N_LAYERS, N_KV, HD, device=dev, generator=g)
-    vn = torch.randn(N_LAYERS, N_KV, HD, device=dev, generator=g)
+        del kr, vr
+    q = torch.randn(n_layers, N_HEADS, HD, device=dev, generator=g)
+    kn = torch.randn(n_layers, N_KV, HD, device=dev, generator=g)
+    vn = torch.randn(n_layers, N_KV, HD, device=dev, generator=g)
     out = torch.empty_like(q)
     ctx.sync()
     torch.cuda.synchronize(dev)
-    pos = CTX - 1
+    pos = ctx_len - 1
 
-    def step(ev=None):
-        for layer in range(N_LAYERS):
-            if ev is not None:
-                ev[layer][0].record(stream)
+    def step():
+        for layer in range(n_layers):
             ctx.decode(layer, pos, q[layer], kn[layer], vn[layer], out[layer])
-            if ev is not None:
-                ev[layer][1].record(stream)
 
     def barrier():
         if world > 1:
@@ -275,50 +275,77 @@ def run_gpu_arm(args):
         step()
     torch.cuda.synchronize(dev)
 
+    # One step (n_layers launches) captured as a CUDA graph, so the timed
+    # region measures the GPU rather than Python's launch rate.
+    graph = None
+    if not args.eager:
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            ctx.bind_torch_stream(side)
+            step()
+        stream.wait_stream(side)
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            ctx.bind_torch_stream()  # the capture stream
+            step()
+        ctx.bind_torch_stream(stream)
+        graph.replay()
+        torch.cuda.synchronize(dev)
+
     # ---- timed region (device time, CUDA events on the launch stream) ------
     sampler = ClockSampler(local)
     sampler.start()
-    launch_ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-                  for _ in range(N_LAYERS)] for _ in range(args.steps)]
     barrier()
     torch.cuda.synchronize(dev)
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
     t_start.record(stream)
-    for k in range(args.steps):
-        step(launch_ev[k])
+    for _ in range(args.steps):
+        if graph is not None:
+            graph.replay()
+        else:
+            step()
     t_end.record(stream)
     torch.cuda.synchronize(dev)
     barrier()
     clocks = sampler.stop()
     ctx.sync()
     elapsed_ms = max_over_ranks(t_start.elapsed_time(t_end))
-    launch_ms = [a.elapsed_time(b) for row in launch_ev for (a, b) in row]
-    mean_launch_ms = max_over_ranks(float(np.mean(launch_ms)))
+    mean_launch_ms = elapsed_ms / (args.steps * n_layers)
 
-    per_launch = algorithmic_bytes(N_HEADS, N_KV, HD, CTX)
-    total_bytes = per_launch * N_LAYERS * args.steps * world
+    per_launch = algorithmic_bytes(N_HEADS, N_KV, HD, ctx_len)
+    total_bytes = per_launch * n_layers * args.steps * world
     value = total_bytes / (elapsed_ms / 1e3) / 1e9
     peak, peak_kind = load_peaks()
     achieved = per_launch / (mean_launch_ms / 1e3) / 1e9
+    del graph
 
     # ---- end to end through the host-pointer entry point -------------------
-    hq = q.cpu().numpy()
-    hk = kn.cpu().numpy()
-    hv = vn.cpu().numpy()
-    ctx.sync()
-    e2e_steps = max(1, args.steps)
-    for _ in range(min(args.warmup, 2)):
-        for layer in range(N_LAYERS):
-            ctx.decode_host(layer, pos, hq[layer], hk[layer], hv[layer])
-    barrier()
-    t0 = time.perf_counter()
-    for _ in range(e2e_steps):
-        for layer in range(N_LAYERS):
-            ctx.decode_host(layer, pos, hq[layer], hk[layer], hv[layer])
-    e2e_s = max_over_ranks(time.perf_counter() - t0)
-    barrier()
-    e2e_value = per_launch * N_LAYERS * e2e_steps * world / e2e_s / 1e9
+    e2e = None
+    if not args.no_e2e:
+        hq = q.cpu().numpy()
+        hk = kn.cpu().numpy()
+        hv = vn.cpu().numpy()
+        ctx.sync()
+        for _ in range(min(args.warmup, 2)):
+            for layer in range(n_layers):
+                ctx.decode_host(layer, pos, hq[layer], hk[layer], hv[layer])
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            for layer in range(n_layers):
+                ctx.decode_host(layer, pos, hq[layer], hk[layer], hv[layer])
+        e2e_s = max_over_ranks(time.perf_counter() - t0)
+        barrier()
+        e2e = {"value": round(per_launch * n_layers * args.steps * world / e2e_s / 1e9, 2),
+               "unit": "GB/s",
+               "h2d_bytes_per_step": int(n_layers * (hq[0].nbytes + hk[0].nbytes
+                                                     + hv[0].nbytes)),
+               "d2h_bytes_per_step": int(n_layers * hq[0].nbytes),
+               "ms_per_step": round(e2e_s / args.steps * 1e3, 4),
+               "path": "leap_attn_decode_host per layer (host buffers, blocking)"}
 
     line = None
     if rank == 0:
@@ -326,13 +353,15 @@ def run_gpu_arm(args):
         tpath = os.path.join(ROOT, "profiles", "decode_attn_traffic.json")
         if os.path.exists(tpath):
             with open(tpath) as f:
-                traffic = json.load(f).get("bytes_per_launch")
+                tr = json.load(f)
+            if tr.get("ctx") == ctx_len:
+                traffic = tr.get("bytes_per_launch")
         line = {
             "metric": "decode-attn KV GB/s", "value": round(value, 2), "unit": "GB/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(elapsed_ms / args.steps, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": workload_config(world),
+            "config": workload_config(world, n_layers, ctx_len),
             "frac_of_hbm_peak": round(value / world / peak, 4),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak,
                          "peak_kind": peak_kind, "unit": "GB/s",
@@ -340,12 +369,8 @@ def run_gpu_arm(args):
                          "kernel": "decode_attn_kernel<128,4>",
                          "bytes_per_launch": per_launch,
                          "mean_launch_us": round(mean_launch_ms * 1e3, 3)},
-            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
-                    "h2d_bytes_per_step": int(N_LAYERS * (hq[0].nbytes + hk[0].nbytes
-                                                          + hv[0].nbytes)),
-                    "d2h_bytes_per_step": int(N_LAYERS * hq[0].nbytes),
-                    "ms_per_step": round(e2e_s / e2e_steps * 1e3, 4)},
-            "gpu_launches": N_LAYERS * args.steps,
+            "e2e": e2e,
+            "gpu_launches": n_layers * args.steps,
             "clocks": clocks,
         }
     ctx.close()
@@ -372,6 +397,10 @@ def main():
     ap.add_argument("--impl", choices=["leap", "reference"], default="leap")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--eager", action="store_true", help="launch from Python, no CUDA graph")
+    ap.add_argument("--layers", type=int, default=N_LAYERS)
+    ap.add_argument("--ctx", type=int, default=CTX)
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "leap":
         args.warmup = 3  # timing rule: at least 3 warm-up steps

@@ -101,9 +101,12 @@ LEAP_API int leap_rope_table(int seq_len, int head_dim, float theta,
 LEAP_API int leap_ctx_create(const leap_ctx_desc *desc, leap_ctx **out);
 LEAP_API int leap_ctx_destroy(leap_ctx *ctx);
 
-/* Use `stream` (a cudaStream_t; NULL = the context's own stream) for all
- * following work of this context. */
+/* Use `stream` (a cudaStream_t; NULL = the CUDA default stream, as
+ * everywhere in CUDA) for all following work of this context. */
 LEAP_API int leap_ctx_set_stream(leap_ctx *ctx, void *stream);
+
+/* Go back to the context's own non-blocking stream (the initial state). */
+LEAP_API int leap_ctx_use_own_stream(leap_ctx *ctx);
 
 /* Block until the context's queued work is done; reports kernel errors. */
 LEAP_API int leap_sync(leap_ctx *ctx);

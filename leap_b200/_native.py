@@ -49,6 +49,7 @@ SIGNATURES: dict[str, tuple] = {
     "leap_ctx_create": (c_int, [ctypes.POINTER(CtxDesc), ctypes.POINTER(c_void_p)]),
     "leap_ctx_destroy": (c_int, [c_void_p]),
     "leap_ctx_set_stream": (c_int, [c_void_p, c_void_p]),
+    "leap_ctx_use_own_stream": (c_int, [c_void_p]),
     "leap_sync": (c_int, [c_void_p]),
     "leap_ctx_device_bytes": (c_int, [c_void_p, ctypes.POINTER(ctypes.c_size_t)]),
     "leap_kv_clear": (c_int, [c_void_p]),

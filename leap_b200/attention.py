@@ -116,7 +116,7 @@ class AttentionContext:
         check(lib().leap_ctx_set_stream(self.handle, ctypes.c_void_p(stream.cuda_stream)))
 
     def use_own_stream(self) -> None:
-        check(lib().leap_ctx_set_stream(self.handle, None))
+        check(lib().leap_ctx_use_own_stream(self.handle))
 
     def sync(self) -> None:
         check(lib().leap_sync(self.handle))

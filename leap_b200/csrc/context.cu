@@ -223,7 +223,8 @@ int leap_ctx_create(const leap_ctx_desc *d, leap_ctx **out) {
 
     c->max_parts = leap::max_decode_parts(c->hd, c->n_kv, c->max_batch, c->max_seq_pad, c->num_sms);
     const size_t po = size_t(c->max_parts) * c->group * c->hd * sizeof(float);
-    const size_t pml = size_t(c->max_parts) * c->group * 2 * sizeof(float);
+    // (M, L) per head per partial, records padded to 16 bytes
+    const size_t pml = size_t(c->max_parts) * 2 * (c->group < 2 ? 2 : c->group) * sizeof(float);
     const size_t cnt = size_t(leap::kMaxSeqPerLaunch) * c->n_kv * sizeof(unsigned);
     if ((e = cudaMalloc(&c->part_o, po)) != cudaSuccess) return fail(e, "cudaMalloc(partials)");
     if ((e = cudaMalloc(&c->part_ml, pml)) != cudaSuccess) return fail(e, "cudaMalloc(partials)");
@@ -253,7 +254,14 @@ int leap_ctx_destroy(leap_ctx *c) {
 int leap_ctx_set_stream(leap_ctx *c, void *stream) {
     leap::clear_error();
     LEAP_CHECK_CTX(c);
-    c->stream = stream ? static_cast<cudaStream_t>(stream) : c->own_stream;
+    c->stream = static_cast<cudaStream_t>(stream);  // NULL: the default stream
+    return LEAP_OK;
+}
+
+int leap_ctx_use_own_stream(leap_ctx *c) {
+    leap::clear_error();
+    LEAP_CHECK_CTX(c);
+    c->stream = c->own_stream;
     return LEAP_OK;
 }
 

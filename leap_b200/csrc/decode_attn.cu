@@ -45,12 +45,14 @@ struct Cfg {
     static constexpr int TILE = kTileBytes / (HD * 4);
     static constexpr int RPG = TILE / NGRP;          // rows per group per tile
     static constexpr int NV4 = G * HD / 4;           // float4 outputs per CTA
+    static constexpr int MLS = 2 * (G < 2 ? 2 : G);  // floats per split's (M, L) record
     static constexpr size_t kSmem = size_t(2) * kStages * TILE * HD * sizeof(float);
     static_assert(DPL % 4 == 0 && C4 >= 1, "lane slice must be float4s");
     static_assert(TILE % NGRP == 0, "tile rows must split over groups");
     // CTA merge buffer [NGRP][G][HD] and combine tables reuse the stages
     static_assert(size_t(NGRP) * G * HD * sizeof(float) <= kSmem, "merge smem");
-    static_assert(size_t(kMaxSplitsPerSeq) * G * 3 * sizeof(float) <= kSmem,
+    // combine staging: (M, L) table + weights + at least one partial
+    static_assert((size_t(kMaxSplitsPerSeq) * (MLS + G) + G * HD) * sizeof(float) <= kSmem,
                   "combine smem");
 };
 
@@ -65,7 +67,7 @@ struct DecodeArgs {
     const float *rope_sin;
     size_t head_stride, layer_off, slot_stride;  // floats
     float *part_o;       // [parts][G*HD]
-    float *part_ml;      // [parts][G][2]
+    float *part_ml;      // [parts][MLS]: (M, L) per head, padded to 16 bytes
     unsigned *counters;  // [kMaxSeqPerLaunch][n_kv]
     int *err;
     int n_kv;
@@ -82,6 +84,7 @@ decode_attn_kernel(const DecodeArgs a, const DecodeSeq tab) {
     __shared__ uint64_t full_bar[kStages];
     __shared__ float red_m[C::NGRP][G], red_l[C::NGRP][G];
     __shared__ float s_M[G], s_L[G];
+    __shared__ uint64_t comb_bar;
     __shared__ int s_last;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -112,6 +115,7 @@ decode_attn_kernel(const DecodeArgs a, const DecodeSeq tab) {
 
     if (tid == 0) {
         for (int s = 0; s < kStages; ++s) mbar_init(&full_bar[s], 1);
+        mbar_init(&comb_bar, 1);
         fence_mbar_init();
     }
     __syncthreads();
@@ -317,7 +321,10 @@ decode_attn_kernel(const DecodeArgs a, const DecodeSeq tab) {
     __syncthreads();
 
     float *out_seq = a.out + (size_t(seq) * a.n_kv * G + qh0) * HD;
-    const int pidx = (tab.split0[seq] + split) * a.n_kv + kvh;
+    // Partials of one (sequence, kv head) are contiguous, so the combining
+    // CTA fetches them with one bulk copy: index kvh * total + split0 + split.
+    const int pfirst = kvh * tab.split0[tab.n_seq] + tab.split0[seq];
+    const int pidx = pfirst + split;
     for (int e = tid; e < C::NV4; e += kThreads) {
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 4
@@ -337,61 +344,102 @@ decode_attn_kernel(const DecodeArgs a, const DecodeSeq tab) {
 
     // ---- split-KV combine by the last CTA of this (sequence, kv head) -----
     if (tid < G) {
-        a.part_ml[(size_t(pidx) * G + tid) * 2 + 0] = s_M[tid];
-        a.part_ml[(size_t(pidx) * G + tid) * 2 + 1] = s_L[tid];
+        a.part_ml[size_t(pidx) * C::MLS + 2 * tid + 0] = s_M[tid];
+        a.part_ml[size_t(pidx) * C::MLS + 2 * tid + 1] = s_L[tid];
     }
-    __threadfence();
     __syncthreads();
     if (tid == 0) {
+        // publish this CTA's partial (release, cumulative over the CTA's
+        // stores ordered by the barrier) and learn whether it is the last
+        fence_proxy_async_global();
         unsigned *cnt = a.counters + seq * a.n_kv + kvh;
-        const unsigned ticket = atomicAdd(cnt, 1u);
+        const unsigned ticket = atom_add_acq_rel_gpu(cnt, 1u);
         s_last = (ticket == unsigned(nsplit - 1));
-        if (s_last) *cnt = 0u;  // ready for the next launch
+        if (s_last) *cnt = 0u;  // ready for the next launch (stream-ordered)
     }
     __syncthreads();
     if (!s_last) return;
-    __threadfence();
 
-    const int pbase = tab.split0[seq] * a.n_kv + kvh;  // split s at pbase + s*n_kv
-    float *cM = sK;                    // [nsplit][G]
-    float *cL = cM + nsplit * G;       // [nsplit][G]
-    float *cW = cL + nsplit * G;       // [nsplit][G]
-    for (int idx = tid; idx < nsplit * G; idx += kThreads) {
-        const int sp = idx / G, g = idx - sp * G;
-        const size_t p = (size_t(pbase) + size_t(sp) * a.n_kv) * G + g;
-        cM[idx] = __ldcg(a.part_ml + 2 * p);
-        cL[idx] = __ldcg(a.part_ml + 2 * p + 1);
+    // Stage the (M, L) table and the partial outputs in shared memory with
+    // bulk copies (one round trip per chunk of partials), then combine.
+    float *sML = sK;                                     // [nsplit][MLS]
+    float *cW = sML + nsplit * C::MLS;                   // [nsplit][G] weights
+    float *sO = cW + ((nsplit * G + 3) & ~3);            // [cap][G*HD]
+    const int cap = int((C::kSmem / sizeof(float) - size_t(sO - sK)) / (G * HD));
+    const int n0 = min(cap, nsplit);
+    uint32_t cphase = 0;
+    if (tid == 0) {
+        fence_proxy_async_global();
+        const uint32_t ml_bytes = uint32_t(nsplit) * C::MLS * 4;
+        const uint32_t o_bytes = uint32_t(n0) * G * HD * 4;
+        mbar_arrive_expect_tx(&comb_bar, ml_bytes + o_bytes);
+        bulk_g2s(sML, a.part_ml + size_t(pfirst) * C::MLS, ml_bytes, &comb_bar);
+        bulk_g2s(sO, a.part_o + size_t(pfirst) * G * HD, o_bytes, &comb_bar);
     }
-    __syncthreads();
-    if (tid < G) {
+    bool cok = mbar_wait(&comb_bar, cphase);
+    cok = __syncthreads_and(cok);
+    if (!cok) {
+        if (tid == 0) report_error(a.err, kDevWaitTimeout);
+        return;
+    }
+    cphase ^= 1u;
+    // one warp per head: max, rescaled sum, normalised weights
+    for (int g = warp; g < G; g += kWarps) {
         float M = -INFINITY;
-        for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, cM[sp * G + tid]);
+        for (int sp = lane; sp < nsplit; sp += 32) M = fmaxf(M, sML[sp * C::MLS + 2 * g]);
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
         float L = 0.f;
-        for (int sp = 0; sp < nsplit; ++sp) L += cL[sp * G + tid] * fast_exp2(cM[sp * G + tid] - M);
-        s_M[tid] = M;
-        s_L[tid] = 1.f / L;
+        for (int sp = lane; sp < nsplit; sp += 32)
+            L += sML[sp * C::MLS + 2 * g + 1] * fast_exp2(sML[sp * C::MLS + 2 * g] - M);
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+        const float inv = 1.f / L;
+        for (int sp = lane; sp < nsplit; sp += 32)
+            cW[sp * G + g] = fast_exp2(sML[sp * C::MLS + 2 * g] - M) * inv;
     }
     __syncthreads();
-    for (int idx = tid; idx < nsplit * G; idx += kThreads) {
-        const int g = idx % G;
-        cW[idx] = fast_exp2(cM[idx] - s_M[g]) * s_L[g];
-    }
-    __syncthreads();
-    for (int e = tid; e < C::NV4; e += kThreads) {
-        const int g = (4 * e) / HD;
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        const float *src = a.part_o + size_t(pbase) * G * HD + 4 * e;
-        const size_t step = size_t(a.n_kv) * G * HD;
-#pragma unroll 4
-        for (int sp = 0; sp < nsplit; ++sp) {
-            const float w = cW[sp * G + g];
-            const float4 v = __ldcg(reinterpret_cast<const float4 *>(src + sp * step));
-            acc.x = fmaf(w, v.x, acc.x);
-            acc.y = fmaf(w, v.y, acc.y);
-            acc.z = fmaf(w, v.z, acc.z);
-            acc.w = fmaf(w, v.w, acc.w);
+    constexpr int kPerThread = (C::NV4 + kThreads - 1) / kThreads;
+    float4 acc[kPerThread];
+#pragma unroll
+    for (int r = 0; r < kPerThread; ++r) acc[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s0 = 0; s0 < nsplit; s0 += cap) {
+        const int n = min(cap, nsplit - s0);
+        if (s0 > 0) {
+            __syncthreads();  // every thread is done with the previous chunk
+            if (tid == 0) {
+                const uint32_t o_bytes = uint32_t(n) * G * HD * 4;
+                mbar_arrive_expect_tx(&comb_bar, o_bytes);
+                bulk_g2s(sO, a.part_o + size_t(pfirst + s0) * G * HD, o_bytes, &comb_bar);
+            }
+            cok = mbar_wait(&comb_bar, cphase);
+            cok = __syncthreads_and(cok);
+            if (!cok) {
+                if (tid == 0) report_error(a.err, kDevWaitTimeout);
+                return;
+            }
+            cphase ^= 1u;
         }
-        *reinterpret_cast<float4 *>(out_seq + 4 * e) = acc;
+#pragma unroll
+        for (int r = 0; r < kPerThread; ++r) {
+            const int e = tid + r * kThreads;
+            if (e < C::NV4) {
+                const int g = (4 * e) / HD;
+                for (int i = 0; i < n; ++i) {
+                    const float w = cW[(s0 + i) * G + g];
+                    const float4 v = *reinterpret_cast<const float4 *>(sO + i * G * HD + 4 * e);
+                    acc[r].x = fmaf(w, v.x, acc[r].x);
+                    acc[r].y = fmaf(w, v.y, acc[r].y);
+                    acc[r].z = fmaf(w, v.z, acc[r].z);
+                    acc[r].w = fmaf(w, v.w, acc[r].w);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < kPerThread; ++r) {
+        const int e = tid + r * kThreads;
+        if (e < C::NV4) *reinterpret_cast<float4 *>(out_seq + 4 * e) = acc[r];
     }
 }
 

@@ -23,7 +23,7 @@ def tables():
 
 
 def _prefill(ctx, slot, layer, pos0, q, k, v, kr=None, vr=None):
-    if pos0:
+    if pos0 and kr is not None:
         ctx.kv_write(slot, layer, 0, kr, vr)
     out = ctx.prefill(slot, layer, pos0, torch.from_numpy(q).cuda(), torch.from_numpy(k).cuda(),
                       torch.from_numpy(v).cuda())
