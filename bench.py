@@ -238,6 +238,9 @@ def run_gpu_arm(args):
 
     n_layers, ctx_len = args.layers, args.ctx
     ctx = AttentionContext(n_layers, N_HEADS, N_KV, HD, ctx_len, device=local, theta=THETA)
+    ctx.set_decode_impl(args.decode_impl)
+    ctx.set_overlap(not args.no_overlap)
+    cluster_cap = ctx.cluster_capacity()
     stream = torch.cuda.current_stream(dev)
     g = torch.Generator(device=dev)
     g.manual_seed(SEED + rank)
@@ -366,7 +369,10 @@ def run_gpu_arm(args):
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak,
                          "peak_kind": peak_kind, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic,
-                         "kernel": "decode_attn_kernel<128,4>",
+                         "kernel": ("decode_cluster_kernel<128,4,16>"
+                                    if (args.decode_impl == 2 or (args.decode_impl == 0
+                                        and cluster_cap >= N_KV))
+                                    else "decode_attn_kernel<128,4>"),
                          "bytes_per_launch": per_launch,
                          "mean_launch_us": round(mean_launch_ms * 1e3, 3)},
             "e2e": e2e,
@@ -399,6 +405,10 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--eager", action="store_true", help="launch from Python, no CUDA graph")
+    ap.add_argument("--decode-impl", type=int, default=0,
+                    help="0 auto, 1 split-KV kernel, 2 cluster kernel")
+    ap.add_argument("--no-overlap", action="store_true",
+                    help="no programmatic dependent launch between layers")
     ap.add_argument("--layers", type=int, default=N_LAYERS)
     ap.add_argument("--ctx", type=int, default=CTX)
     args = ap.parse_args()

@@ -108,6 +108,32 @@ LEAP_API int leap_ctx_set_stream(leap_ctx *ctx, void *stream);
 /* Go back to the context's own non-blocking stream (the initial state). */
 LEAP_API int leap_ctx_use_own_stream(leap_ctx *ctx);
 
+/*
+ * Launch overlap (default on).  A decode launch may start streaming its
+ * layer's K/V cache into shared memory while the previous kernel on the
+ * stream is still finishing (programmatic dependent launch); it reads its
+ * q/k/v inputs and writes anything only after that kernel has completed.
+ * The context turns the overlap off by itself for a launch whose layer the
+ * previous operation of this context wrote (or after leap_kv_write,
+ * leap_kv_clear or a stream change), so results never depend on it.
+ */
+LEAP_API int leap_set_overlap(leap_ctx *ctx, int enable);
+
+/*
+ * Decode kernel selection (results agree within the decode tolerance):
+ *   0 = auto: one sequence uses a 16-CTA thread-block cluster per kv head
+ *       whose split-KV reduction runs in distributed shared memory, when
+ *       every head's cluster fits on the device at once; otherwise the
+ *       split-KV kernel (128-thread CTAs, two per SM) whose last CTA per
+ *       (sequence, kv head) combines the partials;
+ *   1 = that split-KV kernel;  2 = cluster kernel;
+ *   3 = split-KV kernel with 256-thread CTAs, one per SM.
+ */
+LEAP_API int leap_set_decode_impl(leap_ctx *ctx, int impl);
+
+/* Number of 16-CTA decode clusters the device holds at once. */
+LEAP_API int leap_decode_cluster_capacity(const leap_ctx *ctx, int *n);
+
 /* Block until the context's queued work is done; reports kernel errors. */
 LEAP_API int leap_sync(leap_ctx *ctx);
 

@@ -50,6 +50,9 @@ SIGNATURES: dict[str, tuple] = {
     "leap_ctx_destroy": (c_int, [c_void_p]),
     "leap_ctx_set_stream": (c_int, [c_void_p, c_void_p]),
     "leap_ctx_use_own_stream": (c_int, [c_void_p]),
+    "leap_set_overlap": (c_int, [c_void_p, c_int]),
+    "leap_set_decode_impl": (c_int, [c_void_p, c_int]),
+    "leap_decode_cluster_capacity": (c_int, [c_void_p, c_int_p]),
     "leap_sync": (c_int, [c_void_p]),
     "leap_ctx_device_bytes": (c_int, [c_void_p, ctypes.POINTER(ctypes.c_size_t)]),
     "leap_kv_clear": (c_int, [c_void_p]),

@@ -197,6 +197,20 @@ class AttentionContext:
                                       _dptr(q), _dptr(k), _dptr(v), _dptr(out)))
         return out
 
+    def set_decode_impl(self, impl: int) -> None:
+        """0 = auto, 1 = split-KV, 2 = cluster kernel, 3 = wide split-KV."""
+        check(lib().leap_set_decode_impl(self.handle, impl))
+
+    def cluster_capacity(self) -> int:
+        n = ctypes.c_int()
+        check(lib().leap_decode_cluster_capacity(self.handle, ctypes.byref(n)))
+        return n.value
+
+    def set_overlap(self, enable: bool) -> None:
+        """Let a decode launch stream its K/V while the previous kernel
+        finishes (programmatic dependent launch); on by default."""
+        check(lib().leap_set_overlap(self.handle, int(bool(enable))))
+
     def set_prefill_impl(self, impl: int) -> None:
         """0 = tensor-core 3xTF32 kernel, 1 = CUDA-core FP32 kernel."""
         check(lib().leap_set_prefill_impl(self.handle, impl))

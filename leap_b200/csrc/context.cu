@@ -49,9 +49,11 @@ void free_ctx(leap_ctx *c) {
     cudaFree(c->v_cache);
     cudaFree(c->rope_cos);
     cudaFree(c->rope_sin);
-    cudaFree(c->part_o);
-    cudaFree(c->part_ml);
-    cudaFree(c->counters);
+    for (int i = 0; i < 2; ++i) {
+        cudaFree(c->part_o[i]);
+        cudaFree(c->part_ml[i]);
+        cudaFree(c->counters[i]);
+    }
     cudaFree(c->d_stage);
     cudaFree(c->d_qrot);
     if (c->h_stage) cudaFreeHost(c->h_stage);
@@ -86,7 +88,8 @@ int check_device_error(leap_ctx *c) {
     // A CTA that gave up never reached its split-KV ticket: clear the
     // tickets and the error word so the next call starts clean.
     cudaMemset(c->d_err, 0, sizeof(int));
-    cudaMemset(c->counters, 0, sizeof(unsigned) * kMaxSeqPerLaunch * c->n_kv);
+    for (int i = 0; i < 2; ++i)
+        cudaMemset(c->counters[i], 0, sizeof(unsigned) * kMaxSeqPerLaunch * c->n_kv);
     set_error("a kernel reported device error %d (bounded wait timed out)", err);
     return LEAP_ERR_DEVICE;
 }
@@ -226,11 +229,13 @@ int leap_ctx_create(const leap_ctx_desc *d, leap_ctx **out) {
     // (M, L) per head per partial, records padded to 16 bytes
     const size_t pml = size_t(c->max_parts) * 2 * (c->group < 2 ? 2 : c->group) * sizeof(float);
     const size_t cnt = size_t(leap::kMaxSeqPerLaunch) * c->n_kv * sizeof(unsigned);
-    if ((e = cudaMalloc(&c->part_o, po)) != cudaSuccess) return fail(e, "cudaMalloc(partials)");
-    if ((e = cudaMalloc(&c->part_ml, pml)) != cudaSuccess) return fail(e, "cudaMalloc(partials)");
-    if ((e = cudaMalloc(&c->counters, cnt)) != cudaSuccess) return fail(e, "cudaMalloc(counters)");
-    if ((e = cudaMemset(c->counters, 0, cnt)) != cudaSuccess) return fail(e, "cudaMemset(counters)");
-    c->device_bytes += po + pml + cnt;
+    for (int i = 0; i < 2; ++i) {
+        if ((e = cudaMalloc(&c->part_o[i], po)) != cudaSuccess) return fail(e, "cudaMalloc(partials)");
+        if ((e = cudaMalloc(&c->part_ml[i], pml)) != cudaSuccess) return fail(e, "cudaMalloc(partials)");
+        if ((e = cudaMalloc(&c->counters[i], cnt)) != cudaSuccess) return fail(e, "cudaMalloc(counters)");
+        if ((e = cudaMemset(c->counters[i], 0, cnt)) != cudaSuccess) return fail(e, "cudaMemset(counters)");
+    }
+    c->device_bytes += 2 * (po + pml + cnt);
 
     const size_t sb = leap::stage_floats(c) * sizeof(float);
     if ((e = cudaMallocHost(&c->h_stage, sb)) != cudaSuccess) return fail(e, "cudaMallocHost(stage)");
@@ -239,6 +244,10 @@ int leap_ctx_create(const leap_ctx_desc *d, leap_ctx **out) {
     c->d_err = reinterpret_cast<int *>(c->d_stage + leap::stage_floats(c) - 4);
     c->device_bytes += sb;
 
+    if (int cst = leap::decode_cluster_capacity(c, &c->cluster_capacity)) {
+        leap::free_ctx(c);
+        return cst;
+    }
     if ((e = cudaDeviceSynchronize()) != cudaSuccess) return fail(e, "cudaDeviceSynchronize");
     *out = c;
     return LEAP_OK;
@@ -255,6 +264,7 @@ int leap_ctx_set_stream(leap_ctx *c, void *stream) {
     leap::clear_error();
     LEAP_CHECK_CTX(c);
     c->stream = static_cast<cudaStream_t>(stream);  // NULL: the default stream
+    c->last_written_layer = leap_ctx::kWroteAll;   // other work may precede
     return LEAP_OK;
 }
 
@@ -262,6 +272,36 @@ int leap_ctx_use_own_stream(leap_ctx *c) {
     leap::clear_error();
     LEAP_CHECK_CTX(c);
     c->stream = c->own_stream;
+    c->last_written_layer = leap_ctx::kWroteAll;
+    return LEAP_OK;
+}
+
+int leap_set_decode_impl(leap_ctx *c, int impl) {
+    leap::clear_error();
+    LEAP_CHECK_CTX(c);
+    if (impl < 0 || impl > 3) {
+        leap::set_error("decode impl %d unknown", impl);
+        return LEAP_ERR_INVALID;
+    }
+    c->decode_impl = impl;
+    return LEAP_OK;
+}
+
+int leap_decode_cluster_capacity(const leap_ctx *c, int *n) {
+    leap::clear_error();
+    LEAP_CHECK_CTX(c);
+    if (!n) {
+        leap::set_error("null argument");
+        return LEAP_ERR_INVALID;
+    }
+    *n = c->cluster_capacity;
+    return LEAP_OK;
+}
+
+int leap_set_overlap(leap_ctx *c, int enable) {
+    leap::clear_error();
+    LEAP_CHECK_CTX(c);
+    c->overlap = enable ? 1 : 0;
     return LEAP_OK;
 }
 
@@ -287,6 +327,7 @@ int leap_kv_clear(leap_ctx *c) {
     leap::clear_error();
     LEAP_CHECK_CTX(c);
     DeviceGuard g(c->device);
+    c->last_written_layer = leap_ctx::kWroteAll;
     LEAP_TRY_CUDA(cudaMemsetAsync(c->k_cache, 0, c->cache_bytes, c->stream), "clear k");
     LEAP_TRY_CUDA(cudaMemsetAsync(c->v_cache, 0, c->cache_bytes, c->stream), "clear v");
     return LEAP_OK;
@@ -313,6 +354,7 @@ int leap_kv_write(leap_ctx *c, int slot, int layer, int pos0, int n_pos, const f
         return LEAP_ERR_INVALID;
     }
     DeviceGuard g(c->device);
+    c->last_written_layer = leap_ctx::kWroteAll;
     const cudaMemcpyKind kind = from_host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice;
     const size_t row = size_t(c->hd) * sizeof(float);
     for (int h = 0; h < c->n_kv; ++h) {
@@ -388,7 +430,6 @@ int leap_attn_decode(leap_ctx *c, int layer, int pos, const float *q, const floa
     tab.n_seq = 1;
     tab.pos[0] = pos;
     tab.slot[0] = 0;
-    leap::plan_decode(c, tab);
     return leap::launch_decode(c, layer, tab, q, k_new, v_new, out);
 }
 
@@ -418,7 +459,6 @@ int leap_attn_decode_host(leap_ctx *c, int layer, int pos, const float *q, const
     tab.n_seq = 1;
     tab.pos[0] = pos;
     tab.slot[0] = 0;
-    leap::plan_decode(c, tab);
     if (int st = leap::launch_decode(c, layer, tab, dq, dk, dv, dout)) return st;
     // out and the error word come back in one copy
     LEAP_TRY_CUDA(cudaMemcpyAsync(ho, dout, (nq + 4) * sizeof(float), cudaMemcpyDeviceToHost,
@@ -464,8 +504,7 @@ int leap_attn_decode_batched(leap_ctx *c, int layer, int n_seq, const int *slots
             tab.pos[i] = positions[b0 + i];
             tab.slot[i] = slots[b0 + i];
         }
-        leap::plan_decode(c, tab);
-        if (int st = leap::launch_decode(c, layer, tab, q + b0 * nq, k_new + b0 * nk,
+            if (int st = leap::launch_decode(c, layer, tab, q + b0 * nq, k_new + b0 * nk,
                                          v_new + b0 * nk, out + b0 * nq))
             return st;
     }
@@ -484,7 +523,9 @@ int leap_attn_prefill(leap_ctx *c, int slot, int layer, int pos0, int n_tok, con
     }
     if (n_tok == 0) return LEAP_OK;
     DeviceGuard g(c->device);
-    return leap::launch_prefill(c, slot, layer, pos0, n_tok, q, k, v, out);
+    const int st = leap::launch_prefill(c, slot, layer, pos0, n_tok, q, k, v, out);
+    c->last_written_layer = layer;
+    return st;
 }
 
 int leap_set_prefill_impl(leap_ctx *c, int impl) {

@@ -28,11 +28,25 @@ struct leap_ctx {
     // RoPE table [max_seq][hd/2]
     float *rope_cos = nullptr, *rope_sin = nullptr;
 
-    // split-KV scratch
-    float *part_o = nullptr;      // [max_parts][group*hd]
-    float *part_ml = nullptr;     // [max_parts][group][2]
-    unsigned *counters = nullptr; // [max_batch][n_kv]
+    // split-KV scratch, two sets: consecutive decode launches alternate so
+    // that a launch overlapping the previous one's tail never shares it
+    float *part_o[2] = {nullptr, nullptr};      // [max_parts][group*hd]
+    float *part_ml[2] = {nullptr, nullptr};     // [max_parts][2*max(group,2)]
+    unsigned *counters[2] = {nullptr, nullptr}; // [kMaxSeqPerLaunch][n_kv]
     int max_parts = 0;
+    int parity = 0;
+
+    // Launch overlap (programmatic dependent launch): a decode kernel may
+    // start streaming its layer's K/V while the previous kernel finishes,
+    // unless the previous op of this context wrote that layer.
+    int overlap = 1;
+    int last_written_layer = kWroteAll;  // layer the previous op wrote
+    static constexpr int kWroteAll = -2;
+
+    // decode kernel choice: 0 auto, 1 split-KV (global combine),
+    // 2 cluster (distributed-shared-memory combine)
+    int decode_impl = 0;
+    int cluster_capacity = 0;  // co-resident 16-CTA decode clusters
 
     // device error word (kernels report bounded-wait timeouts here)
     int *d_err = nullptr;
@@ -80,13 +94,19 @@ struct DecodeSeq {
     int split0[kMaxSeqPerLaunch + 1];  // prefix sum of splits per sequence
 };
 
-// Launch one batch of decode work (n_seq <= kMaxSeqPerLaunch).  q/k_new/
-// v_new/out point at the first sequence of the batch.
+// Launch one batch of decode work (n_seq <= kMaxSeqPerLaunch; only n_seq,
+// pos and slot of `seqs` need to be set: the split plan is made here).
+// q/k_new/v_new/out point at the first sequence of the batch.
 int launch_decode(leap_ctx *c, int layer, const DecodeSeq &tab, const float *q,
                   const float *k_new, const float *v_new, float *out);
 
 // Fill tab.chunk / tab.split0 for the given positions; returns total splits.
-int plan_decode(const leap_ctx *c, DecodeSeq &tab);
+int plan_decode(const leap_ctx *c, DecodeSeq &tab, int nt);
+
+// decode_cluster.cu: co-resident 16-CTA clusters, and the launch.
+int decode_cluster_capacity(leap_ctx *c, int *n);
+int launch_decode_cluster(leap_ctx *c, int layer, const DecodeSeq &tab, const float *q,
+                          const float *k_new, const float *v_new, float *out, bool overlap);
 
 // Upper bound on split-KV partials one decode launch can need.
 int max_decode_parts(int hd, int n_kv, int max_batch, int max_seq_pad, int num_sms);

@@ -28,21 +28,25 @@
 namespace leap {
 namespace {
 
-constexpr int kThreads = 128;
-constexpr int kWarps = kThreads / 32;
+// Two CTA shapes: NT = 128 threads, 16 KB tiles, two CTAs per SM; or
+// NT = 256 threads, 32 KB tiles, one CTA per SM (half as many splits, so a
+// shorter combine).  Three stages of K+V tiles either way.
 constexpr int kStages = 3;
-constexpr int kTileBytes = 16384;   // per tensor (K or V) per stage
 constexpr int kMaxSplitsPerSeq = 256;
 
-template <int HD, int G>
+template <int HD, int G, int NT>
 struct Cfg {
+    static constexpr int THREADS = NT;
+    static constexpr int WARPS = NT / 32;
+    static constexpr int PER_SM = 256 / NT;           // resident CTAs per SM
+    static constexpr int TILE_BYTES = NT * 128;       // per tensor per stage
     static constexpr int kLpr0 = G * HD / 64;
     static constexpr int LPR = kLpr0 < 8 ? 8 : (kLpr0 > 32 ? 32 : kLpr0);
     static constexpr int RPW = 32 / LPR;             // rows per warp pass
-    static constexpr int NGRP = kWarps * RPW;        // row groups per CTA
+    static constexpr int NGRP = WARPS * RPW;        // row groups per CTA
     static constexpr int DPL = HD / LPR;             // dims per lane
     static constexpr int C4 = DPL / 4;               // float4 chunks per lane
-    static constexpr int TILE = kTileBytes / (HD * 4);
+    static constexpr int TILE = TILE_BYTES / (HD * 4);
     static constexpr int RPG = TILE / NGRP;          // rows per group per tile
     static constexpr int NV4 = G * HD / 4;           // float4 outputs per CTA
     static constexpr int MLS = 2 * (G < 2 ? 2 : G);  // floats per split's (M, L) record
@@ -74,10 +78,10 @@ struct DecodeArgs {
     float scale_log2;    // log2(e) / sqrt(HD)
 };
 
-template <int HD, int G>
-__global__ void __launch_bounds__(kThreads, 2)
+template <int HD, int G, int NT>
+__global__ void __launch_bounds__(NT, 256 / NT)
 decode_attn_kernel(const DecodeArgs a, const DecodeSeq tab) {
-    using C = Cfg<HD, G>;
+    using C = Cfg<HD, G, NT>;
     extern __shared__ __align__(128) unsigned char smem_raw[];
     float *sK = reinterpret_cast<float *>(smem_raw);      // [kStages][TILE][HD]
     float *sV = sK + kStages * C::TILE * HD;
@@ -129,6 +133,11 @@ decode_attn_kernel(const DecodeArgs a, const DecodeSeq tab) {
             bulk_g2s(sV + t * C::TILE * HD, gV + size_t(r0) * HD, bytes, &full_bar[t]);
         }
     }
+    // Up to here only this layer's cache rows were read, which the previous
+    // kernel of the stream never writes (the host launches with overlap only
+    // then).  Inputs, scratch and outputs may still be in use by it.
+    grid_dependency_wait();
+    grid_launch_dependents();
 
     // ---- rotated q slice: heads kvh*G .. +G, dims of this lane's chunks ---
     const int qh0 = kvh * G;
@@ -180,7 +189,7 @@ decode_attn_kernel(const DecodeArgs a, const DecodeSeq tab) {
             const int rr = pos - r0;
             const float *kn = a.k_new + (size_t(seq) * a.n_kv + kvh) * HD;
             const float *vn = a.v_new + (size_t(seq) * a.n_kv + kvh) * HD;
-            for (int d = 2 * tid; d < HD; d += 2 * kThreads) {
+            for (int d = 2 * tid; d < HD; d += 2 * C::THREADS) {
                 const float2 kk = *reinterpret_cast<const float2 *>(kn + d);
                 const float2 vv = *reinterpret_cast<const float2 *>(vn + d);
                 const float2 kr = rope_pair(kk.x, kk.y, rc[d / 2], rs[d / 2]);
@@ -325,7 +334,7 @@ decode_attn_kernel(const DecodeArgs a, const DecodeSeq tab) {
     // CTA fetches them with one bulk copy: index kvh * total + split0 + split.
     const int pfirst = kvh * tab.split0[tab.n_seq] + tab.split0[seq];
     const int pidx = pfirst + split;
-    for (int e = tid; e < C::NV4; e += kThreads) {
+    for (int e = tid; e < C::NV4; e += C::THREADS) {
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 4
         for (int gg = 0; gg < C::NGRP; ++gg) {
@@ -384,7 +393,7 @@ decode_attn_kernel(const DecodeArgs a, const DecodeSeq tab) {
     }
     cphase ^= 1u;
     // one warp per head: max, rescaled sum, normalised weights
-    for (int g = warp; g < G; g += kWarps) {
+    for (int g = warp; g < G; g += C::WARPS) {
         float M = -INFINITY;
         for (int sp = lane; sp < nsplit; sp += 32) M = fmaxf(M, sML[sp * C::MLS + 2 * g]);
 #pragma unroll
@@ -399,7 +408,7 @@ decode_attn_kernel(const DecodeArgs a, const DecodeSeq tab) {
             cW[sp * G + g] = fast_exp2(sML[sp * C::MLS + 2 * g] - M) * inv;
     }
     __syncthreads();
-    constexpr int kPerThread = (C::NV4 + kThreads - 1) / kThreads;
+    constexpr int kPerThread = (C::NV4 + C::THREADS - 1) / C::THREADS;
     float4 acc[kPerThread];
 #pragma unroll
     for (int r = 0; r < kPerThread; ++r) acc[r] = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -422,7 +431,7 @@ decode_attn_kernel(const DecodeArgs a, const DecodeSeq tab) {
         }
 #pragma unroll
         for (int r = 0; r < kPerThread; ++r) {
-            const int e = tid + r * kThreads;
+            const int e = tid + r * C::THREADS;
             if (e < C::NV4) {
                 const int g = (4 * e) / HD;
                 for (int i = 0; i < n; ++i) {
@@ -438,33 +447,43 @@ decode_attn_kernel(const DecodeArgs a, const DecodeSeq tab) {
     }
 #pragma unroll
     for (int r = 0; r < kPerThread; ++r) {
-        const int e = tid + r * kThreads;
+        const int e = tid + r * C::THREADS;
         if (e < C::NV4) *reinterpret_cast<float4 *>(out_seq + 4 * e) = acc[r];
     }
 }
 
-template <int HD, int G>
-int launch_t(leap_ctx *c, const DecodeArgs &a, const DecodeSeq &tab, int total_splits) {
-    using C = Cfg<HD, G>;
+template <int HD, int G, int NT>
+int launch_t(leap_ctx *c, const DecodeArgs &a, const DecodeSeq &tab, int total_splits,
+             bool overlap) {
+    using C = Cfg<HD, G, NT>;
     static bool attr_set[kMaxDevices] = {};  // the attribute is per device
     if (c->device >= kMaxDevices) return cuda_status(cudaErrorInvalidDevice, "device");
     if (!attr_set[c->device]) {
-        cudaError_t e = cudaFuncSetAttribute(decode_attn_kernel<HD, G>,
+        cudaError_t e = cudaFuncSetAttribute(decode_attn_kernel<HD, G, NT>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              int(C::kSmem));
         if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(decode)");
         attr_set[c->device] = true;
     }
-    dim3 grid(total_splits, c->n_kv);
-    decode_attn_kernel<HD, G><<<grid, kThreads, C::kSmem, c->stream>>>(a, tab);
-    return cuda_status(cudaGetLastError(), "decode_attn_kernel launch");
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(total_splits, c->n_kv);
+    cfg.blockDim = dim3(NT);
+    cfg.dynamicSmemBytes = C::kSmem;
+    cfg.stream = c->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = overlap ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cuda_status(cudaLaunchKernelEx(&cfg, decode_attn_kernel<HD, G, NT>, a, tab),
+                       "decode_attn_kernel launch");
 }
 
 }  // namespace
 
-int plan_decode(const leap_ctx *c, DecodeSeq &tab) {
-    const int tile = kTileBytes / (c->hd * 4);
-    const long cap_rows = 262144L / (c->hd * 4 * 2);  // ~256 KB of K+V per CTA
+int plan_decode(const leap_ctx *c, DecodeSeq &tab, int nt) {
+    const int tile = nt * 128 / (c->hd * 4);
+    const long cap_rows = 2048L * nt / (c->hd * 4 * 2);  // 256/512 KB of K+V per CTA
     long total = 0;
     int max_ctx = 0;
     for (int i = 0; i < tab.n_seq; ++i) {
@@ -473,7 +492,7 @@ int plan_decode(const leap_ctx *c, DecodeSeq &tab) {
         if (ctx > max_ctx) max_ctx = ctx;
     }
     const long rows = total * c->n_kv;
-    const long target = 2L * c->num_sms;  // one wave at two CTAs per SM
+    const long target = long(256 / nt) * c->num_sms;  // one wave
     long chunk = (rows + target - 1) / target;
     if (chunk > cap_rows) chunk = cap_rows;
     const long min_chunk = (max_ctx + kMaxSplitsPerSeq - 1) / kMaxSplitsPerSeq;
@@ -490,15 +509,55 @@ int plan_decode(const leap_ctx *c, DecodeSeq &tab) {
 }
 
 int max_decode_parts(int hd, int n_kv, int max_batch, int max_seq_pad, int num_sms) {
-    const long cap_rows = 262144L / (hd * 4 * 2);
+    const long cap_rows = 262144L / (hd * 4 * 2);  // the narrow CTA shape needs most
     const long nb = max_batch < kMaxSeqPerLaunch ? max_batch : kMaxSeqPerLaunch;
     long a = (nb * max_seq_pad * long(n_kv) + cap_rows - 1) / cap_rows;
     if (a < 2L * num_sms) a = 2L * num_sms;
     return int(a + nb * n_kv * 2 + 64);
 }
 
-int launch_decode(leap_ctx *c, int layer, const DecodeSeq &tab, const float *q,
+namespace {
+template <int NT>
+int launch_width(leap_ctx *c, const DecodeArgs &a, const DecodeSeq &tab, int total, bool overlap) {
+    switch (c->hd * 100 + c->group) {
+        case 12801: return launch_t<128, 1, NT>(c, a, tab, total, overlap);
+        case 12802: return launch_t<128, 2, NT>(c, a, tab, total, overlap);
+        case 12804: return launch_t<128, 4, NT>(c, a, tab, total, overlap);
+        case 12808: return launch_t<128, 8, NT>(c, a, tab, total, overlap);
+        case 6401: return launch_t<64, 1, NT>(c, a, tab, total, overlap);
+        case 6402: return launch_t<64, 2, NT>(c, a, tab, total, overlap);
+        case 6404: return launch_t<64, 4, NT>(c, a, tab, total, overlap);
+        case 6408: return launch_t<64, 8, NT>(c, a, tab, total, overlap);
+        default:
+            set_error("unsupported head_dim %d / kv_mul %d", c->hd, c->group);
+            return LEAP_ERR_INVALID;
+    }
+}
+}  // namespace
+
+int launch_decode(leap_ctx *c, int layer, const DecodeSeq &seqs, const float *q,
                   const float *k_new, const float *v_new, float *out) {
+    // Overlap with the previous kernel only if this context's previous
+    // operation did not write this layer (the early K/V prefetch must not
+    // read rows that kernel may still be appending).
+    const bool overlap = c->overlap && c->last_written_layer != leap_ctx::kWroteAll &&
+                         c->last_written_layer != layer;
+    // decode_impl 2 forces the cluster kernel (16 CTAs per kv head, split
+    // reduction in distributed shared memory); auto never picks it unless
+    // every head's cluster fits at once.
+    const bool use_cluster =
+        c->decode_impl == 2 ||
+        (c->decode_impl == 0 && seqs.n_seq == 1 && c->cluster_capacity >= c->n_kv);
+    if (use_cluster) {
+        const int st = launch_decode_cluster(c, layer, seqs, q, k_new, v_new, out, overlap);
+        if (st == LEAP_OK) c->last_written_layer = layer;
+        return st;
+    }
+    // Split-KV CTA shape: 128 threads, two CTAs per SM (measured fastest at
+    // ctx 1k-8k); impl 3 selects 256 threads, one per SM (half the splits).
+    const int nt = (c->decode_impl == 3) ? 256 : 128;
+    DecodeSeq tab = seqs;
+    plan_decode(c, tab, nt);
     const int total = tab.split0[tab.n_seq];
     if (long(total) * c->n_kv > c->max_parts) {
         set_error("decode plan needs %d partials, scratch holds %d", total * c->n_kv,
@@ -517,26 +576,21 @@ int launch_decode(leap_ctx *c, int layer, const DecodeSeq &tab, const float *q,
     a.head_stride = c->head_stride;
     a.layer_off = size_t(layer) * c->layer_stride;
     a.slot_stride = c->slot_stride;
-    a.part_o = c->part_o;
-    a.part_ml = c->part_ml;
-    a.counters = c->counters;
+    // alternate scratch sets so an overlapped launch never shares the
+    // previous launch's partials or tickets
+    a.part_o = c->part_o[c->parity];
+    a.part_ml = c->part_ml[c->parity];
+    a.counters = c->counters[c->parity];
     a.err = c->d_err;
     a.n_kv = c->n_kv;
     a.scale_log2 = kLog2e / sqrtf(float(c->hd));
-    const int key = c->hd * 100 + c->group;
-    switch (key) {
-        case 12801: return launch_t<128, 1>(c, a, tab, total);
-        case 12802: return launch_t<128, 2>(c, a, tab, total);
-        case 12804: return launch_t<128, 4>(c, a, tab, total);
-        case 12808: return launch_t<128, 8>(c, a, tab, total);
-        case 6401: return launch_t<64, 1>(c, a, tab, total);
-        case 6402: return launch_t<64, 2>(c, a, tab, total);
-        case 6404: return launch_t<64, 4>(c, a, tab, total);
-        case 6408: return launch_t<64, 8>(c, a, tab, total);
-        default:
-            set_error("unsupported head_dim %d / kv_mul %d", c->hd, c->group);
-            return LEAP_ERR_INVALID;
+    const int st = nt == 128 ? launch_width<128>(c, a, tab, total, overlap)
+                             : launch_width<256>(c, a, tab, total, overlap);
+    if (st == LEAP_OK) {
+        c->parity ^= 1;
+        c->last_written_layer = layer;
     }
+    return st;
 }
 
 }  // namespace leap

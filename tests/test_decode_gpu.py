@@ -34,7 +34,11 @@ def _run(ctx, layer, pos, q, kn, vn, kr, vr):
     return out.cpu().numpy(), kk[0], vv[0]
 
 
-def test_decode_golden(cuda, golden):
+IMPLS = [1, 2, 3]  # split-KV (the auto choice here), cluster kernel, wide split-KV
+
+
+@pytest.mark.parametrize("impl", IMPLS)
+def test_decode_golden(cuda, golden, impl):
     data, man = golden
     ctxs = {}
     for case in man["decode"]:
@@ -42,6 +46,7 @@ def test_decode_golden(cuda, golden):
         h, kv, hd = SHAPES[shape]
         if shape not in ctxs:
             ctxs[shape] = AttentionContext(1, h, kv, hd, 1100)
+            ctxs[shape].set_decode_impl(impl)
         q, kn, vn, kr, vr = decode_inputs(shape, pos, case["seed"])
         out, krow, vrow = _run(ctxs[shape], 0, pos, q, kn, vn, kr, vr)
         key = f"decode/{shape}/{pos}"
@@ -53,13 +58,15 @@ def test_decode_golden(cuda, golden):
         c.close()
 
 
+@pytest.mark.parametrize("impl", IMPLS)
 @pytest.mark.parametrize("ctx_len", [1024, 4096, 8192])
-def test_decode_config2_l8b(cuda, tables, ctx_len):
+def test_decode_config2_l8b(cuda, tables, ctx_len, impl):
     """Llama-3-8B heads, one query at ctx 1024/4096/8192."""
     h, kv, hd = SHAPES["l8b"]
     pos = ctx_len - 1
     q, kn, vn, kr, vr = decode_inputs("l8b", pos, 2000 + ctx_len)
     with AttentionContext(1, h, kv, hd, 8192) as ctx:
+        ctx.set_decode_impl(impl)
         out, krow, _ = _run(ctx, 0, pos, q, kn, vn, kr, vr)
     c, s = tables[hd]
     ref, kref = oracle.decode_case(q, kn, vn, kr, vr, pos, h, kv, hd, c, s, threads=8)
@@ -67,13 +74,15 @@ def test_decode_config2_l8b(cuda, tables, ctx_len):
     np.testing.assert_array_equal(krow, kref)
 
 
+@pytest.mark.parametrize("impl", IMPLS)
 @pytest.mark.parametrize("shape", ["tl", "l70b", "mha128", "g2_64"])
-def test_decode_shapes_long(cuda, tables, shape):
+def test_decode_shapes_long(cuda, tables, shape, impl):
     """Every head layout at a context long enough for many splits."""
     h, kv, hd = SHAPES[shape]
     pos = 5000
     q, kn, vn, kr, vr = decode_inputs(shape, pos, 77)
     with AttentionContext(1, h, kv, hd, 6000) as ctx:
+        ctx.set_decode_impl(impl)
         out, krow, _ = _run(ctx, 0, pos, q, kn, vn, kr, vr)
     c, s = tables[hd]
     ref, kref = oracle.decode_case(q, kn, vn, kr, vr, pos, h, kv, hd, c, s, threads=8)
@@ -81,12 +90,16 @@ def test_decode_shapes_long(cuda, tables, shape):
     np.testing.assert_array_equal(krow, kref)
 
 
-def test_decode_split_and_tile_edges(cuda, tables):
-    """Positions on both sides of tile (32 rows) and split boundaries."""
+@pytest.mark.parametrize("impl", IMPLS)
+def test_decode_split_and_tile_edges(cuda, tables, impl):
+    """Positions on both sides of tile (32/64 rows) and split boundaries,
+    and contexts shorter than the cluster (some CTAs own no rows)."""
     h, kv, hd = SHAPES["l8b"]
     c, s = tables[hd]
     with AttentionContext(1, h, kv, hd, 4096) as ctx:
-        for pos in (31, 32, 33, 63, 64, 223, 224, 225, 447, 448, 2047, 2048, 4095):
+        ctx.set_decode_impl(impl)
+        for pos in (2, 14, 15, 16, 31, 32, 33, 63, 64, 65, 223, 224, 225, 447, 448, 1023,
+                    1024, 2047, 2048, 4095):
             q, kn, vn, kr, vr = decode_inputs("l8b", pos, 31 + pos)
             out, krow, _ = _run(ctx, 0, pos, q, kn, vn, kr, vr)
             ref, kref = oracle.decode_case(q, kn, vn, kr, vr, pos, h, kv, hd, c, s, threads=8)
@@ -94,7 +107,8 @@ def test_decode_split_and_tile_edges(cuda, tables):
             np.testing.assert_array_equal(krow, kref)
 
 
-def test_decode_consecutive_steps(cuda, tables):
+@pytest.mark.parametrize("impl", IMPLS)
+def test_decode_consecutive_steps(cuda, tables, impl):
     """Token-by-token decode: the cache grows through the kernel's own
     appends, as forward() does in the reference (main.cpp:80-89)."""
     h, kv, hd = SHAPES["tl"]
@@ -104,6 +118,7 @@ def test_decode_consecutive_steps(cuda, tables):
     kc = np.zeros((n, kv * hd), np.float32)
     vc = np.zeros((n, kv * hd), np.float32)
     with AttentionContext(2, h, kv, hd, 128) as ctx:
+        ctx.set_decode_impl(impl)
         for pos in range(n):
             q = rng.standard_normal((h, hd), dtype=np.float32)
             kn = rng.standard_normal((kv, hd), dtype=np.float32)
@@ -122,6 +137,57 @@ def test_decode_consecutive_steps(cuda, tables):
         # layer 0 was never touched
         k0, _ = ctx.kv_read(0, 0, 0, n)
         assert not k0.any()
+
+
+@pytest.mark.parametrize("impl", IMPLS)
+@pytest.mark.parametrize("overlap", [True, False])
+def test_decode_layer_chain_overlap(cuda, tables, overlap, impl):
+    """Launch overlap: layer l's decode takes layer l-1's output as its q
+    (so it must read q only after the previous kernel completed), layers
+    alternate, and every step grows the caches; checked step by step."""
+    h, kv, hd = SHAPES["l8b"]
+    c, s = tables[hd]
+    n_layers, n_steps, pos0 = 4, 6, 700
+    rng = np.random.default_rng(17)
+    kc = [np.zeros((pos0 + n_steps, kv * hd), np.float32) for _ in range(n_layers)]
+    vc = [np.zeros((pos0 + n_steps, kv * hd), np.float32) for _ in range(n_layers)]
+    with AttentionContext(n_layers, h, kv, hd, pos0 + n_steps) as ctx:
+        ctx.set_overlap(overlap)
+        ctx.set_decode_impl(impl)
+        for layer in range(n_layers):
+            kr = rng.standard_normal((pos0, kv, hd), dtype=np.float32)
+            vr = rng.standard_normal((pos0, kv, hd), dtype=np.float32)
+            ctx.kv_write(0, layer, 0, kr, vr)
+            kc[layer][:pos0] = kr.reshape(pos0, -1)
+            vc[layer][:pos0] = vr.reshape(pos0, -1)
+        for step in range(n_steps):
+            pos = pos0 + step
+            x = rng.standard_normal((h, hd), dtype=np.float32)
+            xd = _dev(x)
+            news = []
+            outs = []
+            for layer in range(n_layers):
+                kn = rng.standard_normal((kv, hd), dtype=np.float32)
+                vn = rng.standard_normal((kv, hd), dtype=np.float32)
+                xd = ctx.decode(layer, pos, xd, _dev(kn), _dev(vn))  # no sync between layers
+                news.append((kn, vn))
+                outs.append(xd)
+            got = [o.cpu().numpy() for o in outs]
+            for layer in range(n_layers):
+                kn, vn = news[layer]
+                kc[layer][pos] = kn.reshape(-1)
+                vc[layer][pos] = vn.reshape(-1)
+                # the oracle is fed the GPU's own input for this layer, so
+                # errors do not compound through the chain; it rotates the
+                # running cache row in place like the reference
+                ref_in = x if layer == 0 else got[layer - 1]
+                ref = oracle.attn_block(ref_in.reshape(-1).copy(), kc[layer], vc[layer], pos, h,
+                                        kv, hd, c, s).reshape(h, hd)
+                assert rel_err(got[layer], ref) <= TOL, (step, layer)
+        ctx.sync()
+        for layer in range(n_layers):
+            kk, _ = ctx.kv_read(0, layer, pos0, n_steps)
+            np.testing.assert_array_equal(kk.reshape(n_steps, -1), kc[layer][pos0:])
 
 
 def test_decode_host_entry_point_matches_device(cuda):
@@ -159,3 +225,12 @@ def test_clear_kv_cache(cuda):
         ctx.sync()
         k, v = ctx.kv_read(0, 0, 0, 10)
         assert not k.any() and not v.any()
+
+
+def test_cluster_capacity_query(cuda):
+    """The context reports how many 16-CTA decode clusters fit at once (7 on
+    the B200s measured here: one GPC has fewer than 16 usable SMs), and auto
+    mode picks the cluster kernel only when every kv head's cluster fits."""
+    h, kv, hd = SHAPES["l8b"]
+    with AttentionContext(1, h, kv, hd, 64) as ctx:
+        assert ctx.cluster_capacity() >= 1
