@@ -206,6 +206,45 @@ LEAP_API int leap_attn_prefill(leap_ctx *ctx, int slot, int layer, int pos0, int
                       const float *q, const float *k, const float *v,
                       float *out);
 
+/*
+ * Decode attention that allocates nothing.  (No counterpart in the
+ * reference: LEAP's CPU engine owns all its memory in std::vectors.)
+ *
+ * For callers that cannot call cudaMalloc: a host whose device memory is all
+ * owned by one allocator or a fixed arena, code being recorded into a stream
+ * or graph that must not change the device's allocations, or an embedding
+ * that is not allowed to touch CUDA's allocator.  Such a caller cannot create
+ * a leap_ctx (which allocates the cache and scratch), so this entry point
+ * takes everything as caller-owned device memory and keeps its own scratch
+ * (split-KV partials, combine tickets, an error word) in a 4 MiB array
+ * compiled into the library, which every GPU that loads the library holds
+ * until the process exits.  It calls no cudaMalloc, cudaFree or other
+ * allocating routine.
+ *
+ * Same computation as leap_attn_decode for one token at `pos`, with the
+ * caller's cache: k_cache/v_cache are [n_kv_heads][head_stride] floats, row t
+ * of kv head h at k_cache + h*head_stride + t*head_dim, rows 0..pos-1
+ * already rotated; row pos is written (rotated k, raw v).  rope_cos/rope_sin
+ * are device tables [>= pos+1][head_dim/2] (leap_rope_table's values).  All
+ * pointers device, 16-byte aligned; head_stride a multiple of 4 floats and
+ * >= (pos+1)*head_dim.  Runs on `stream` (NULL = default stream).
+ *
+ * The first call on a device looks up the array's device address (once per
+ * device), so make that first call before any stream capture.  Every call
+ * shares the one array and clears the part of it that must start at zero;
+ * calls that overlap on the GPU (different streams, or different host
+ * threads) race on it and must not be issued.  A context too long for the
+ * scratch (more split-KV partials than fit in 4 MiB, about 64k positions
+ * for 8 kv heads of 4x128) is rejected with LEAP_ERR_INVALID and a message.
+ */
+LEAP_API int leap_attn_decode_noalloc(void *stream, int n_heads, int n_kv_heads,
+                                      int head_dim, int pos,
+                                      const float *rope_cos,
+                                      const float *rope_sin, float *k_cache,
+                                      float *v_cache, long long head_stride,
+                                      const float *q, const float *k_new,
+                                      const float *v_new, float *out);
+
 /* Prefill kernel selection (for tests and benchmarks):
  *   0 = default (tensor-core 3xTF32 path), 1 = CUDA-core FP32 path. */
 LEAP_API int leap_set_prefill_impl(leap_ctx *ctx, int impl);

@@ -69,6 +69,9 @@ SIGNATURES: dict[str, tuple] = {
     "leap_attn_prefill": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p,
                                   c_void_p, c_void_p, c_void_p]),
     "leap_set_prefill_impl": (c_int, [c_void_p, c_int]),
+    "leap_attn_decode_noalloc": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p,
+                                         c_void_p, c_void_p, c_void_p, ctypes.c_longlong,
+                                         c_void_p, c_void_p, c_void_p, c_void_p]),
 }
 
 _lock = threading.Lock()
