@@ -56,6 +56,23 @@ def algorithmic_bytes(n_heads, n_kv, hd, ctx):
                 + n_heads * hd)
 
 
+def read_traffic(ctx):
+    """DRAM bytes (read + write) per decode launch from the committed ncu
+    launch-list summary, or None when none was captured for this context."""
+    p = os.path.join(ROOT, "profiles", "decode_attn_kernel_l8b_ctx8192.traffic.txt")
+    if not os.path.exists(p):
+        return None
+    kv = {}
+    with open(p) as f:
+        for line in f:
+            if "=" in line and not line.lstrip().startswith("#"):
+                k, v = line.split("=", 1)
+                kv[k.strip()] = v.strip()
+    if int(kv.get("ctx", -1)) != ctx:
+        return None
+    return int(kv["bytes_per_launch"])
+
+
 def load_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -352,13 +369,7 @@ def run_gpu_arm(args):
 
     line = None
     if rank == 0:
-        traffic = None
-        tpath = os.path.join(ROOT, "profiles", "decode_attn_traffic.json")
-        if os.path.exists(tpath):
-            with open(tpath) as f:
-                tr = json.load(f)
-            if tr.get("ctx") == ctx_len:
-                traffic = tr.get("bytes_per_launch")
+        traffic = read_traffic(ctx_len)
         line = {
             "metric": "decode-attn KV GB/s", "value": round(value, 2), "unit": "GB/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
