@@ -406,6 +406,59 @@ def run_gpu_arm(args):
         print(json.dumps(line), flush=True)
 
 
+def run_prefill(args):
+    """causal prefill, Llama-3-8B heads, batch 1, prompt
+    length L.  One step = the prefill of L tokens of one layer (RoPE + append
+    + causal attention), cycling 8 layers so K/V (8 x 8 x L x 1 KB) are not
+    all L2-resident.  Metric: logical TFLOP/s, FLOP = 2*n_h*hd*L*(L+1)."""
+    import torch
+    from leap_b200 import AttentionContext
+    dev = torch.device("cuda", 0)
+    L, n_layers = args.prefill, 8
+    ctx = AttentionContext(n_layers, N_HEADS, N_KV, HD, L, theta=THETA)
+    ctx.set_prefill_impl(args.prefill_impl)
+    g = torch.Generator(device=dev)
+    g.manual_seed(2)
+    q = torch.randn(L, N_HEADS, HD, device=dev, generator=g)
+    k = torch.randn(L, N_KV, HD, device=dev, generator=g)
+    v = torch.randn(L, N_KV, HD, device=dev, generator=g)
+    out = torch.empty_like(q)
+    stream = torch.cuda.current_stream(dev)
+    for i in range(max(args.warmup, 3)):
+        ctx.prefill(0, i % n_layers, 0, q, k, v, out)
+    torch.cuda.synchronize(dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        ctx.prefill(0, i % n_layers, 0, q, k, v, out)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ctx.sync()
+    ms = e0.elapsed_time(e1) / args.steps
+    flop = 2.0 * N_HEADS * HD * L * (L + 1)
+    tflops = flop / (ms / 1e3) / 1e12
+    peak = 1622.9
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            peak = float(json.load(f)["bf16_tflops"])
+    line = {"metric": "causal prefill TFLOP/s (logical FP32)", "value": round(tflops, 2),
+            "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 4), "higher_is_better": True, "dtype": "f32 (3xTF32)"
+            if args.prefill_impl == 0 else "f32",
+            "config": {"workload": f"config4: causal prefill L={L}, Llama-3-8B heads, batch 1",
+                       "seq_len": L, "impl": "tcgen05 3xTF32" if args.prefill_impl == 0
+                       else "CUDA-core FP32"},
+            "roofline": {"bound": "tensor", "achieved": round(tflops, 2),
+                         "tensor_tflops_issued": round(3 * tflops, 2)
+                         if args.prefill_impl == 0 else None,
+                         "peak": peak, "peak_kind": "measured bf16 dense (TF32 is half)",
+                         "unit": "TFLOP/s", "frac": round(tflops / peak, 4)}}
+    ctx.close()
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -420,6 +473,10 @@ def main():
                     help="0 auto, 1 split-KV kernel, 2 cluster kernel")
     ap.add_argument("--no-overlap", action="store_true",
                     help="no programmatic dependent launch between layers")
+    ap.add_argument("--prefill", type=int, default=0,
+                    help="benchmark config 4 (causal prefill of this many tokens) instead")
+    ap.add_argument("--prefill-impl", type=int, default=0,
+                    help="0 tcgen05 3xTF32, 1 CUDA-core FP32")
     ap.add_argument("--layers", type=int, default=N_LAYERS)
     ap.add_argument("--ctx", type=int, default=CTX)
     args = ap.parse_args()
@@ -427,6 +484,8 @@ def main():
         args.warmup = 3  # timing rule: at least 3 warm-up steps
     if args.impl == "reference":
         run_reference_arm(args)
+    elif args.prefill:
+        run_prefill(args)
     else:
         run_gpu_arm(args)
 
