@@ -245,9 +245,116 @@ LEAP_API int leap_attn_decode_noalloc(void *stream, int n_heads, int n_kv_heads,
                                       const float *q, const float *k_new,
                                       const float *v_new, float *out);
 
+/* ======================================================================
+ * The forward pass around attention (decode-step driver).
+ *
+ * leap_engine holds the weights of a contiguous layer range of a LEAP model
+ * on one GPU — all layers for the single-process engine, or one pipeline
+ * stage's range (the split of src/inference/Transformer.h:17-23) — plus
+ * that range's KV cache.  It reads the reference's own .bin files (v0/v1
+ * FP32, v2 W8A8: src/inference/TransformerFactory.cpp:59-135, weight order
+ * of FloatTransformer.cpp:947-978 / QuantizedTransformer.cpp:102-134) and
+ * runs, per layer, what run_layer does (FloatTransformer.cpp:384-749,
+ * QuantizedTransformer.cpp:654-1012) on sm_100a kernels.
+ * ====================================================================== */
+
+typedef struct leap_model_config {
+    /* src/inference/Config.h:5-13 */
+    int dim, hidden_dim, n_layers, n_heads, n_kv_heads, vocab_size, seq_len;
+    int quantized;         /* 0: FP32 (.bin v0/v1); 1: W8A8 (.bin v2)       */
+    int group_size;        /* W8A8 quantization group (v2 header)            */
+    int shared_classifier; /* classifier tied to the token embedding         */
+} leap_model_config;
+
+typedef struct leap_engine leap_engine; /* opaque */
+
+/*
+ * Load layers [layer_begin, layer_end) of the model file at `path` onto
+ * `device` (layer_end = -1: to the last layer).  The range holding layer 0
+ * also holds the embedding; the range holding the last layer also holds the
+ * final norm and the classifier.  rope_theta 0 = the reference's hard-coded
+ * 500000 (FloatTransformer.cpp:65).  max_chunk = the most prompt tokens one
+ * leap_engine_layers call takes (0 = 512).
+ */
+LEAP_API int leap_engine_open(const char *path, int device, int layer_begin,
+                              int layer_end, float rope_theta, int max_chunk,
+                              leap_engine **out);
+
+/* Same, with N(0, 0.02) weights (RMSNorm weights 1) generated on the device
+ * from `seed` — for shapes too large to write to a file. */
+LEAP_API int leap_engine_synthetic(const leap_model_config *cfg,
+                                   unsigned long long seed, int device,
+                                   int layer_begin, int layer_end,
+                                   float rope_theta, int max_chunk,
+                                   leap_engine **out);
+
+LEAP_API int leap_engine_destroy(leap_engine *e);
+LEAP_API int leap_engine_config(const leap_engine *e, leap_model_config *cfg,
+                                int *layer_begin, int *layer_end);
+LEAP_API int leap_engine_device_bytes(const leap_engine *e, size_t *bytes);
+LEAP_API int leap_engine_set_stream(leap_engine *e, void *stream);
+LEAP_API int leap_engine_sync(leap_engine *e);
+
+/* Transformer::clear_kv_cache (FloatTransformer.cpp:74-77). */
+LEAP_API int leap_engine_clear_kv(leap_engine *e);
+
+/* Stage operations on device buffers (asynchronous on the engine stream):
+ *   embed:  x[n][dim] <- embedding rows of tokens[0..n) (host ints)
+ *   layers: this engine's layers on x[n][dim] in place, for positions
+ *           pos0..pos0+n-1 (n = 1 is the decode step; n > 1 a prompt chunk,
+ *           n <= max_chunk)
+ *   head:   final RMSNorm of x[dim] (in place, as the reference), classifier
+ *           into logits[vocab] (device, or NULL) and the greedy token into
+ *           *token (device int, or NULL). */
+LEAP_API int leap_engine_embed(leap_engine *e, const int *tokens, int n, float *x);
+LEAP_API int leap_engine_layers(leap_engine *e, int pos0, int n, float *x);
+LEAP_API int leap_engine_head(leap_engine *e, float *x, float *logits, int *token);
+
+/* Transformer::forward(token, pos) of a single-stage engine
+ * (FloatTransformer.cpp:751-797): logits[vocab] into host memory (or
+ * NULL) and the greedy next token (Sampler at temperature 0,
+ * src/inference/Sampler.cpp:199-202) into *next_token (or NULL). Blocks. */
+LEAP_API int leap_engine_forward(leap_engine *e, int token, int pos,
+                                 float *logits, int *next_token);
+
+/* Prefill of n prompt tokens at pos0.. through a single-stage engine in
+ * chunks of max_chunk; *next_token = greedy token after the last one. */
+LEAP_API int leap_engine_prefill(leap_engine *e, const int *tokens, int n,
+                                 int pos0, int *next_token);
+
 /* Prefill kernel selection (for tests and benchmarks):
  *   0 = default (tensor-core 3xTF32 path), 1 = CUDA-core FP32 path. */
 LEAP_API int leap_set_prefill_impl(leap_ctx *ctx, int impl);
+
+/* ---- support ops of the layer, one kernel each --------------------------
+ * Device pointers, stream-ordered on `stream` (NULL = default stream).  The
+ * engine above launches exactly these; they are exported so that each one
+ * can be checked against the reference function it replaces. */
+
+/* rows x rmsnorm over `dim` (FloatTransformer.cpp:79-214): o = w * x *
+ * 1/sqrt(mean(x^2) + 1e-5).  o may equal x. */
+LEAP_API int leap_op_rmsnorm(void *stream, float *o, const float *x,
+                             const float *w, int rows, int dim);
+/* Activation quantize (QuantizedTransformer.cpp:338-357): per group of gs,
+ * s = max|x| * (1/127), q = round(x / s).  n % gs == 0. */
+LEAP_API int leap_op_quantize(void *stream, int8_t *q, float *s,
+                              const float *x, long long n, int gs);
+/* y[t][d] = W[d][n] . x[t] (+ res[t]) in FP32 for T tokens
+ * (FloatTransformer.cpp:240-382 per token); T == 1 is the decode GEMV,
+ * T > 1 the prompt-chunk GEMM.  res may equal y. */
+LEAP_API int leap_op_matmul(void *stream, float *y, const float *x,
+                            const float *w, int n, int d, int T,
+                            const float *res);
+/* W8A8 grouped GEMV/GEMM (QuantizedTransformer.cpp:359-652 per token):
+ * y[t][i] = sum over groups g, in order, of (int32 dot of group g) *
+ * ws[i][g] * xs[t][g]; gs == 64.  res may equal y. */
+LEAP_API int leap_op_qmatmul(void *stream, float *y, const int8_t *xq,
+                             const float *xs, const int8_t *wq,
+                             const float *ws, int n, int d, int T, int gs,
+                             const float *res);
+/* Greedy sampling (Sampler.cpp:20-120 at temperature 0): index of the
+ * first maximum in the reference's scan order. */
+LEAP_API int leap_op_argmax(void *stream, int *token, const float *v, int n);
 
 #ifdef __cplusplus
 }

@@ -41,6 +41,13 @@ class CtxDesc(ctypes.Structure):
     ]
 
 
+class ModelConfigC(ctypes.Structure):
+    """``leap_model_config`` (include/leap_b200.h)."""
+    _fields_ = [(n, c_int) for n in ("dim", "hidden_dim", "n_layers", "n_heads", "n_kv_heads",
+                                     "vocab_size", "seq_len", "quantized", "group_size",
+                                     "shared_classifier")]
+
+
 # name -> (restype, argtypes); every symbol include/leap_b200.h declares
 SIGNATURES: dict[str, tuple] = {
     "leap_last_error": (ctypes.c_char_p, []),
@@ -72,6 +79,30 @@ SIGNATURES: dict[str, tuple] = {
     "leap_attn_decode_noalloc": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p,
                                          c_void_p, c_void_p, c_void_p, ctypes.c_longlong,
                                          c_void_p, c_void_p, c_void_p, c_void_p]),
+    "leap_engine_open": (c_int, [ctypes.c_char_p, c_int, c_int, c_int, ctypes.c_float, c_int,
+                                 ctypes.POINTER(c_void_p)]),
+    "leap_engine_synthetic": (c_int, [ctypes.POINTER(ModelConfigC), ctypes.c_ulonglong, c_int,
+                                      c_int, c_int, ctypes.c_float, c_int,
+                                      ctypes.POINTER(c_void_p)]),
+    "leap_engine_destroy": (c_int, [c_void_p]),
+    "leap_engine_config": (c_int, [c_void_p, ctypes.POINTER(ModelConfigC), c_int_p, c_int_p]),
+    "leap_engine_device_bytes": (c_int, [c_void_p, ctypes.POINTER(ctypes.c_size_t)]),
+    "leap_engine_set_stream": (c_int, [c_void_p, c_void_p]),
+    "leap_engine_sync": (c_int, [c_void_p]),
+    "leap_engine_clear_kv": (c_int, [c_void_p]),
+    "leap_engine_embed": (c_int, [c_void_p, c_int_p, c_int, c_void_p]),
+    "leap_engine_layers": (c_int, [c_void_p, c_int, c_int, c_void_p]),
+    "leap_engine_head": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p]),
+    "leap_engine_forward": (c_int, [c_void_p, c_int, c_int, c_float_p, c_int_p]),
+    "leap_engine_prefill": (c_int, [c_void_p, c_int_p, c_int, c_int, c_int_p]),
+    "leap_op_rmsnorm": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int]),
+    "leap_op_quantize": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, ctypes.c_longlong,
+                                 c_int]),
+    "leap_op_matmul": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
+                               c_void_p]),
+    "leap_op_qmatmul": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                c_int, c_int, c_int, c_int, c_void_p]),
+    "leap_op_argmax": (c_int, [c_void_p, c_void_p, c_void_p, c_int]),
 }
 
 _lock = threading.Lock()

@@ -38,7 +38,6 @@ template <int HD, int G, int NT>
 struct Cfg {
     static constexpr int THREADS = NT;
     static constexpr int WARPS = NT / 32;
-    static constexpr int PER_SM = 256 / NT;           // resident CTAs per SM
     static constexpr int TILE_BYTES = NT * 128;       // per tensor per stage
     static constexpr int kLpr0 = G * HD / 64;
     static constexpr int LPR = kLpr0 < 8 ? 8 : (kLpr0 > 32 ? 32 : kLpr0);

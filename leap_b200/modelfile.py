@@ -1,0 +1,142 @@
+"""LEAP model files (.bin): header parsing and seeded synthetic writers.
+
+Layouts follow the reference exporter and loader:
+
+* v1 FP32 — ``src/export/Export.cpp:17-93``: magic ``0x616B3432``, int32
+  version 1, the 7-int ``Config`` (``src/inference/Config.h:5-13``), a
+  shared-classifier byte, zero padding to 256 bytes, then attention norms,
+  FFN norms, final norm, token embeddings, wq, wk, wv, wo, w1, w2, w3 (each
+  for all layers in turn) and the classifier if not shared.  The reference
+  loader ties the classifier whenever ``vocab_size > 0``
+  (``src/inference/TransformerFactory.cpp:115-118``), so these files are
+  written tied.
+* v2 W8A8 — ``Export.cpp:95-274``: the same header plus an int32 group size,
+  FP32 norms, then per tensor ``int8[numel]`` followed by
+  ``float32[numel / group_size]`` for the embeddings, wq..w3 per layer, and
+  the classifier if not shared.  Quantization follows
+  ``src/export/Utils.cpp:58-85``: ``s = max|w| / 127``,
+  ``q = round_half_away(w * (1/s))``.
+
+Synthetic weights are N(0, 0.02) from ``numpy.random.default_rng`` seeded per
+tensor, RMSNorm weights 1.0 — the BASELINE configs' description.
+"""
+from __future__ import annotations
+
+import dataclasses
+import hashlib
+import struct
+
+import numpy as np
+
+MAGIC = 0x616B3432
+
+
+@dataclasses.dataclass
+class ModelConfig:
+    dim: int
+    hidden_dim: int
+    n_layers: int
+    n_heads: int
+    n_kv_heads: int
+    vocab_size: int
+    seq_len: int
+
+    @property
+    def head_dim(self) -> int:
+        return self.dim // self.n_heads
+
+    @property
+    def kv_dim(self) -> int:
+        return self.n_kv_heads * self.head_dim
+
+    def as_tuple(self):
+        return (self.dim, self.hidden_dim, self.n_layers, self.n_heads, self.n_kv_heads,
+                self.vocab_size, self.seq_len)
+
+
+def read_header(path: str):
+    """(ModelConfig, quantized, group_size, shared_classifier, header_bytes),
+    as TransformerFactory.cpp:59-118 reads it."""
+    with open(path, "rb") as f:
+        b = f.read(256)
+    (magic,) = struct.unpack_from("<i", b, 0)
+    quantized, gs, shared = 0, 0, 0
+    if magic == MAGIC:
+        (version,) = struct.unpack_from("<i", b, 4)
+        cfg = struct.unpack_from("<7i", b, 8)
+        if version == 1:
+            hdr = 256
+        elif version == 2:
+            quantized = 1
+            shared = b[36]
+            (gs,) = struct.unpack_from("<i", b, 37)
+            hdr = 256
+        else:
+            raise ValueError(f"Bad file version {version}")
+    else:
+        cfg = struct.unpack_from("<7i", b, 0)
+        hdr = 28
+    cfg = list(cfg)
+    if not quantized:
+        shared = 1 if cfg[5] > 0 else 0
+        cfg[5] = abs(cfg[5])
+    return ModelConfig(*cfg), quantized, gs, shared, hdr
+
+
+def _rng(seed: int, name: str):
+    h = hashlib.sha256(f"{seed}/{name}".encode()).digest()
+    return np.random.default_rng(int.from_bytes(h[:8], "little"))
+
+
+def _normal(seed, name, shape, std=0.02):
+    return (_rng(seed, name).standard_normal(shape, dtype=np.float32) * np.float32(std))
+
+
+def quantize_q80(w: np.ndarray, gs: int):
+    """src/export/Utils.cpp:58-85 on a flat float32 array."""
+    g = w.reshape(-1, gs)
+    wmax = np.abs(g).max(axis=1).astype(np.float32)
+    s = (wmax / np.float32(127.0)).astype(np.float32)
+    inv = np.where(s != 0, np.float32(1.0) / np.where(s != 0, s, np.float32(1)), np.float32(0))
+    v = (g * inv[:, None].astype(np.float32)).astype(np.float32)
+    q = (np.sign(v) * np.floor(np.abs(v) + np.float32(0.5))).astype(np.int8)
+    return q.reshape(-1), s
+
+
+def _tensors(cfg: ModelConfig, seed: int):
+    """(name, shape) in file order for the per-layer weight matrices."""
+    L, d, h, kv = cfg.n_layers, cfg.dim, cfg.hidden_dim, cfg.kv_dim
+    order = []
+    for kind, shape in (("wq", (d, d)), ("wk", (kv, d)), ("wv", (kv, d)), ("wo", (d, d)),
+                        ("w1", (h, d)), ("w2", (d, h)), ("w3", (h, d))):
+        for l in range(L):
+            order.append((f"{kind}.{l}", shape))
+    return order
+
+
+def write_v1(path: str, cfg: ModelConfig, seed: int = 0) -> None:
+    """Synthetic FP32 model (tied classifier)."""
+    with open(path, "wb") as f:
+        hdr = struct.pack("<Ii", MAGIC, 1) + struct.pack("<7i", *cfg.as_tuple()) + bytes([1])
+        f.write(hdr + bytes(256 - len(hdr)))
+        ones = np.ones(cfg.dim, np.float32)
+        for _ in range(2 * cfg.n_layers + 1):
+            f.write(ones.tobytes())
+        f.write(_normal(seed, "tok", (cfg.vocab_size, cfg.dim)).tobytes())
+        for name, shape in _tensors(cfg, seed):
+            f.write(_normal(seed, name, shape).tobytes())
+
+
+def write_v2(path: str, cfg: ModelConfig, seed: int = 0, group_size: int = 64) -> None:
+    """Synthetic W8A8 model (tied classifier)."""
+    with open(path, "wb") as f:
+        hdr = (struct.pack("<Ii", MAGIC, 2) + struct.pack("<7i", *cfg.as_tuple()) + bytes([1])
+               + struct.pack("<i", group_size))
+        f.write(hdr + bytes(256 - len(hdr)))
+        ones = np.ones(cfg.dim, np.float32)
+        for _ in range(2 * cfg.n_layers + 1):
+            f.write(ones.tobytes())
+        for name, shape in [("tok", (cfg.vocab_size, cfg.dim))] + _tensors(cfg, seed):
+            q, s = quantize_q80(_normal(seed, name, shape).reshape(-1), group_size)
+            f.write(q.tobytes())
+            f.write(s.tobytes())

@@ -201,3 +201,139 @@ def prefill(q, k, v, k_rows, v_rows, pos0, n_heads, n_kv_heads, head_size,
                             _p(va), _p(kc), _p(vc), _p(out), threads)
     return (out, kc.reshape(seq_len, n_kv_heads, head_size),
             vc.reshape(seq_len, n_kv_heads, head_size))
+
+
+# --------------------------------------------------------------------------
+# The unmodified reference engine (Transformer::create / forward), compiled
+# from its sources into oracle/_ref (ref_engine_glue.cpp).
+# --------------------------------------------------------------------------
+
+class RefEngine:
+    """The reference engine on a .bin file: forward(token, pos) -> logits.
+
+    theta_10k selects the copy built with the RoPE literal set to 10000
+    (TinyLlama); the shipped reference hard-codes 500000."""
+
+    def __init__(self, path: str, theta_10k: bool = False):
+        so = REF_ENGINE_10K_SO if theta_10k else REF_ENGINE_SO
+        if not os.path.exists(so):
+            raise FileNotFoundError(f"{so} missing: run `make -C oracle ref`")
+        lib = _load(so)
+        lib.leapref_engine_create.restype = ctypes.c_void_p
+        lib.leapref_engine_create.argtypes = [ctypes.c_char_p]
+        lib.leapref_engine_forward.restype = _f
+        lib.leapref_engine_forward.argtypes = [ctypes.c_void_p, _int, _int]
+        lib.leapref_engine_config.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int)]
+        lib.leapref_engine_clear.argtypes = [ctypes.c_void_p]
+        lib.leapref_engine_destroy.argtypes = [ctypes.c_void_p]
+        lib.leapref_engine_error.restype = ctypes.c_char_p
+        lib.leapref_sample_argmax.argtypes = [_f, _int]
+        self.lib = lib
+        self.h = lib.leapref_engine_create(path.encode())
+        if not self.h:
+            raise RuntimeError(lib.leapref_engine_error().decode())
+        cfg = (ctypes.c_int * 7)()
+        lib.leapref_engine_config(self.h, cfg)
+        self.config = tuple(cfg)
+
+    def forward(self, token: int, pos: int) -> np.ndarray:
+        p = self.lib.leapref_engine_forward(self.h, token, pos)
+        if not p:
+            raise RuntimeError(self.lib.leapref_engine_error().decode())
+        return np.ctypeslib.as_array(p, shape=(self.config[5],)).copy()
+
+    def argmax(self, logits: np.ndarray) -> int:
+        a = np.ascontiguousarray(logits, np.float32)
+        return int(self.lib.leapref_sample_argmax(_p(a), int(a.size)))
+
+    def clear(self):
+        self.lib.leapref_engine_clear(self.h)
+
+    def close(self):
+        if self.h:
+            self.lib.leapref_engine_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def ref_argmax(v) -> int:
+    """Greedy token through the reference Sampler (temperature 0)."""
+    a = np.ascontiguousarray(v, np.float32)
+    lib = _load(REF_ENGINE_SO)
+    lib.leapref_sample_argmax.argtypes = [_f, _int]
+    return int(lib.leapref_sample_argmax(_p(a), int(a.size)))
+
+
+def has_ref_engine() -> bool:
+    return os.path.exists(REF_ENGINE_SO) and os.path.exists(REF_ENGINE_10K_SO)
+
+
+# --------------------------------------------------------------------------
+# Support ops of the layer (end-to-end configs): port and reference
+# --------------------------------------------------------------------------
+
+def ref_support() -> ctypes.CDLL:
+    lib = ref_attn()
+    lib.leapref_rmsnorm.argtypes = [_f, _f, _f, _int]
+    lib.leapref_matmul.argtypes = [_f, _f, _f, _int, _int]
+    lib.leapref_quantize.argtypes = [_int, _i8, _f, _f, _int]
+    lib.leapref_dequantize.argtypes = [_int, _f, _i8, _f, _int]
+    lib.leapref_qmatmul.argtypes = [_int, _f, _i8, _f, _i8, _f, _int, _int]
+    return lib
+
+
+def rmsnorm(x, w, impl: str = "port"):
+    """FloatTransformer.cpp:79-214 on one row."""
+    x = np.ascontiguousarray(x, np.float32)
+    w = np.ascontiguousarray(w, np.float32)
+    o = np.empty_like(x)
+    if impl == "port":
+        port().orc_rmsnorm(_p(o), _p(x), _p(w), int(x.size))
+    else:
+        ref_support().leapref_rmsnorm(_p(o), _p(x), _p(w), int(x.size))
+    return o
+
+
+def matmul(x, w, impl: str = "port", threads: int = 1):
+    """y[d] = W[d][n] . x (FloatTransformer.cpp:240-382)."""
+    x = np.ascontiguousarray(x, np.float32)
+    w = np.ascontiguousarray(w, np.float32)
+    d, n = w.shape
+    y = np.empty(d, np.float32)
+    if impl == "port":
+        port().orc_matmul(_p(y), _p(x), _p(w), n, d, threads)
+    else:
+        ref_support().leapref_matmul(_p(y), _p(x), _p(w), n, d)
+    return y
+
+
+def quantize(x, gs: int = 64, impl: str = "port"):
+    """(q int8[n], s float32[n/gs]) — QuantizedTransformer.cpp:338-357."""
+    x = np.ascontiguousarray(x, np.float32).reshape(-1)
+    q = np.empty(x.size, np.int8)
+    s = np.empty(x.size // gs, np.float32)
+    if impl == "port":
+        port().orc_quantize(_p(q), _p(s), _p(x), int(x.size), gs)
+    else:
+        ref_support().leapref_quantize(gs, _p(q), _p(s), _p(x), int(x.size))
+    return q, s
+
+
+def qmatmul(xq, xs, wq, ws, gs: int = 64, impl: str = "port", threads: int = 1):
+    """W8A8 GEMV y[d] (QuantizedTransformer.cpp:359-652); wq [d][n]."""
+    xq = np.ascontiguousarray(xq, np.int8)
+    xs = np.ascontiguousarray(xs, np.float32)
+    wq = np.ascontiguousarray(wq, np.int8)
+    ws = np.ascontiguousarray(ws, np.float32)
+    d, n = wq.shape
+    y = np.empty(d, np.float32)
+    if impl == "port":
+        port().orc_qmatmul(_p(y), _p(xq), _p(xs), _p(wq), _p(ws), n, d, gs, threads)
+    else:
+        ref_support().leapref_qmatmul(gs, _p(y), _p(xq), _p(xs), _p(wq), _p(ws), n, d)
+    return y

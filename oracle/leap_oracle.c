@@ -90,7 +90,18 @@ static float dot_avx2_order(const float *a, const float *b, int n) {
     const float t0 = acc[0] + acc[4], t1 = acc[1] + acc[5];
     const float t2 = acc[2] + acc[6], t3 = acc[3] + acc[7];
     float r = (t0 + t1) + (t2 + t3);
-    for (; i < n; i++) r += a[i] * b[i];
+    /* Scalar tail (:330-339 / :375-377).  The release build (-O3
+     * -ffast-math) turns 4 or more leftover elements into one 4-wide step:
+     * separately rounded products, summed (p0+p2)+(p1+p3) and added to the
+     * running value; the rest become fma.  Checked against the compiled
+     * reference for tails of 1..7. */
+    if (n - i >= 4) {
+        const float p0 = a[i] * b[i], p1 = a[i + 1] * b[i + 1];
+        const float p2 = a[i + 2] * b[i + 2], p3 = a[i + 3] * b[i + 3];
+        r = r + ((p0 + p2) + (p1 + p3));
+        i += 4;
+    }
+    for (; i < n; i++) r = fmaf(a[i], b[i], r);
     return r;
 }
 
@@ -202,8 +213,14 @@ void orc_matmul(float *xout, const float *x, const float *w, int n, int d,
 
 /* QuantizedTransformer.cpp:338-357 (same math as the exporter,
  * src/export/Utils.cpp:58-85).  std::round rounds half away from zero,
- * which is C roundf. */
+ * which is C roundf.  The source computes scale = max / 127.0f and
+ * id = 1.0f / scale; the reference's release build (-ffast-math) evaluates
+ * them as scale = max * (1/127) and id = 127 / max (checked against the
+ * compiled reference: the source's quotient differs in the last bit for ~5%
+ * of groups, and 1/scale moves a code across a rounding boundary about once
+ * in 10^5 values).  This follows the compiled form. */
 void orc_quantize(int8_t *q, float *s, const float *x, int n, int gs) {
+    const float inv127 = 1.0f / 127.0f;
     for (int i = 0; i < n; i += gs) {
         const int cur = (gs < n - i) ? gs : n - i;
         float max_val = 0.0f;
@@ -211,15 +228,18 @@ void orc_quantize(int8_t *q, float *s, const float *x, int n, int gs) {
             const float a = fabsf(x[i + j]);
             if (a > max_val) max_val = a;
         }
-        const float scale = max_val / 127.0f;
-        const float id = scale != 0.0f ? 1.0f / scale : 0.0f;
+        const float scale = max_val * inv127;
+        const float id = scale != 0.0f ? 127.0f / max_val : 0.0f;
         s[i / gs] = scale;
         for (int j = 0; j < cur; j++) q[i + j] = (int8_t)roundf(x[i + j] * id);
     }
 }
 
 /* QuantizedTransformer.cpp:359-652: per output row, groups in order; the
- * int32 group dot is exact, then val += float(ival) * w_s * x_s. */
+ * int32 group dot is exact, then val += float(ival) * w_s * x_s, which the
+ * reference's release build evaluates as val = fma(float(ival), w_s*x_s, val)
+ * (bit-exact against the compiled reference; the literal left-to-right
+ * order matches only ~30% of outputs). */
 void orc_qmatmul(float *xout, const int8_t *xq, const float *xs,
                  const int8_t *wq, const float *ws, int n, int d, int gs,
                  int n_threads) {
@@ -234,7 +254,8 @@ void orc_qmatmul(float *xout, const int8_t *xq, const float *xs,
             int32_t ival = 0;
             for (int k = 0; k < gs; k++)
                 ival += (int32_t)xq[j + k] * (int32_t)wq[in + j + k];
-            val += (float)ival * ws[(in + j) / gs] * xs[j / gs];
+            const float t = ws[(in + j) / gs] * xs[j / gs];
+            val = fmaf((float)ival, t, val);
         }
         xout[i] = val;
     }

@@ -12,6 +12,12 @@
 //                and a copy with the literal set to 10000 for TinyLlama)
 //   W8A8 block   src/inference/QuantizedTransformer.cpp:680-923
 //   W8A8 softmax src/inference/QuantizedTransformer.cpp:314-336
+// and the support ops around the block, for kernel-level parity:
+//   fp32 rmsnorm    src/inference/FloatTransformer.cpp:79-214
+//   fp32 matmul     src/inference/FloatTransformer.cpp:240-382
+//   W8A8 dequantize src/inference/QuantizedTransformer.cpp:136-216
+//   W8A8 quantize   src/inference/QuantizedTransformer.cpp:338-357
+//   W8A8 matmul     src/inference/QuantizedTransformer.cpp:359-652
 // This file compiles them, with the reference's release flags, inside a
 // scope that supplies what run_layer() would have in scope (p, s,
 // k / k_cache_ptr, loff, kv_dim, kv_mul, head_size, pos, rope_cos,
@@ -43,14 +49,31 @@ struct FloatTransformer {
     std::vector<float> rope_cos, rope_sin;
     void precompute_freqs();
     static void softmax(float *x, int size);
+    static void rmsnorm(float *o, const float *x, const float *weight, int size);
+    static void matmul(float *xout, const float *x, const float *w, int n, int d);
 };
 #include "fp32_softmax.inc"
 #include "fp32_rope.inc"
+#include "fp32_rmsnorm.inc"
+#include "fp32_matmul.inc"
+
+struct QuantizedTensor {
+    int8_t *q;
+    float *s;
+};
 
 struct QuantizedTransformer {
+    int group_size = 64;
     static void softmax(float *x, int size);
+    void dequantize(const QuantizedTensor *qx, float *x, int n) const;
+    void quantize(const QuantizedTensor *qx, const float *x, int n) const;
+    void matmul(float *xout, const QuantizedTensor *x, const QuantizedTensor *w, int n,
+                int d) const;
 };
 #include "w8a8_softmax.inc"
+#include "w8a8_dequantize.inc"
+#include "w8a8_quantize.inc"
+#include "w8a8_matmul.inc"
 
 struct Fp32Block : FloatTransformer {
     static void run(const Inference::Config *p, RunStateView *s, float *k,
@@ -110,6 +133,35 @@ extern "C" void leapref_attn_block(int which, int n_heads, int n_kv_heads,
     else
         leapref::W8A8Block::run(&cfg, &s, krow, 0, kv_dim, kv_mul, head_size,
                                 pos, rope_cos, rope_sin);
+}
+
+// The reference's support ops around the block (FloatTransformer.cpp:79-214
+// rmsnorm, :240-382 matmul; QuantizedTransformer.cpp:136-216 dequantize,
+// :338-357 quantize, :359-652 int8 matmul), for kernel-level parity.
+extern "C" void leapref_rmsnorm(float *o, const float *x, const float *w, int n) {
+    leapref::FloatTransformer::rmsnorm(o, x, w, n);
+}
+extern "C" void leapref_matmul(float *xout, const float *x, const float *w, int n, int d) {
+    leapref::FloatTransformer::matmul(xout, x, w, n, d);
+}
+extern "C" void leapref_quantize(int gs, int8_t *q, float *s, const float *x, int n) {
+    leapref::QuantizedTransformer t;
+    t.group_size = gs;
+    leapref::QuantizedTensor qt{q, s};
+    t.quantize(&qt, x, n);
+}
+extern "C" void leapref_dequantize(int gs, float *x, int8_t *q, float *s, int n) {
+    leapref::QuantizedTransformer t;
+    t.group_size = gs;
+    leapref::QuantizedTensor qt{q, s};
+    t.dequantize(&qt, x, n);
+}
+extern "C" void leapref_qmatmul(int gs, float *xout, int8_t *xq, float *xs, int8_t *wq,
+                                float *ws, int n, int d) {
+    leapref::QuantizedTransformer t;
+    t.group_size = gs;
+    leapref::QuantizedTensor xt{xq, xs}, wt{wq, ws};
+    t.matmul(xout, &xt, &wt, n, d);
 }
 
 // The reference's RoPE table for a model of `dim`/`n_heads`/`seq_len`,

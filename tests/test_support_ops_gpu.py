@@ -1,0 +1,177 @@
+"""GPU: the support ops of the layer against the C restatement of the
+reference functions they replace, each called through its C-ABI entry point
+(leap_op_*), which launches the same kernel the engine launches.
+
+Bit-exact: activation quantize (QuantizedTransformer.cpp:338-357), the W8A8
+GEMV/GEMM (:359-652, 4-row blocks) and argmax (Sampler.cpp:20-120).
+Tolerance: FP32 GEMV/GEMM (FloatTransformer.cpp:240-382) and rmsnorm
+(:79-214), whose sums the GPU associates differently: per output
+4 sqrt(n) eps sum|w x| (GEMV/GEMM) and 1e-6 of max|ref| (rmsnorm).
+"""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from leap_b200._native import LeapError, check, lib
+
+pytestmark = pytest.mark.gpu
+
+
+def _s():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def _quantize_dev(x_d, gs=64):
+    n = x_d.numel()
+    q = torch.empty(n, dtype=torch.int8, device=x_d.device)
+    s = torch.empty(n // gs, dtype=torch.float32, device=x_d.device)
+    check(lib().leap_op_quantize(_s(), q.data_ptr(), s.data_ptr(), x_d.data_ptr(), n, gs))
+    return q, s
+
+
+@pytest.mark.parametrize("n", [64, 4096, 14336, 28672 * 3])
+def test_quantize_bit_exact(cuda, n):
+    r = np.random.default_rng(n)
+    x = (r.standard_normal(n) * 3).astype(np.float32)
+    if n > 256:
+        x[:64] = 0                       # an all-zero group (scale 0)
+        x[64:128] = np.float32(1e-30)    # a tiny group
+        x[200] = np.float32(-1e4)        # one large value
+    q, s = _quantize_dev(_dev(x))
+    torch.cuda.synchronize()
+    q0, s0 = oracle.quantize(x)
+    assert np.array_equal(q.cpu().numpy(), q0)
+    assert np.array_equal(s.cpu().numpy().view(np.uint32), s0.view(np.uint32))
+
+
+def _qmm(xq, xs, wq, ws, n, d, T, res=None):
+    y = torch.empty((T, d), dtype=torch.float32, device="cuda")
+    check(lib().leap_op_qmatmul(_s(), y.data_ptr(), xq.data_ptr(), xs.data_ptr(), wq.data_ptr(),
+                                ws.data_ptr(), n, d, T, 64,
+                                res.data_ptr() if res is not None else None))
+    return y
+
+
+@pytest.mark.parametrize("n,d", [(2048, 256), (4096, 6144), (14336, 4096), (8192, 1024),
+                                 (28672, 256), (65536, 64)])
+def test_qmatmul_gemv_bit_exact(cuda, n, d):
+    r = np.random.default_rng(n * 7 + d)
+    x = r.standard_normal(n).astype(np.float32)
+    w = (r.standard_normal((d, n)) * 0.02).astype(np.float32)
+    wq, ws = oracle.quantize(w.reshape(-1))
+    xq_d, xs_d = _quantize_dev(_dev(x))
+    y = _qmm(xq_d, xs_d, _dev(wq), _dev(ws), n, d, 1)
+    torch.cuda.synchronize()
+    xq, xs = oracle.quantize(x)
+    ref = oracle.qmatmul(xq, xs, wq.reshape(d, n), ws.reshape(d, n // 64), threads=8)
+    assert np.array_equal(y.cpu().numpy()[0], ref)
+
+
+@pytest.mark.parametrize("T", [2, 33, 100])
+def test_qmatmul_gemm_equals_gemv_rows(cuda, T):
+    n, d = 4096, 1024 + 64
+    r = np.random.default_rng(T)
+    x = r.standard_normal((T, n)).astype(np.float32)
+    w = (r.standard_normal((d, n)) * 0.02).astype(np.float32)
+    res = r.standard_normal((T, d)).astype(np.float32)
+    wq, ws = oracle.quantize(w.reshape(-1))
+    wq_d, ws_d = _dev(wq), _dev(ws)
+    xq_d, xs_d = _quantize_dev(_dev(x))
+    y = _qmm(xq_d, xs_d, wq_d, ws_d, n, d, T, _dev(res))
+    rows = [_qmm(xq_d[t * n:(t + 1) * n], xs_d[t * n // 64:(t + 1) * n // 64], wq_d, ws_d,
+                 n, d, 1, _dev(res[t])) for t in range(T)]
+    torch.cuda.synchronize()
+    y = y.cpu().numpy()
+    for t in range(T):
+        assert np.array_equal(y[t], rows[t].cpu().numpy()[0])
+    # and against the port, with the residual added after the group chain
+    xq, xs = oracle.quantize(x[-1])
+    ref = oracle.qmatmul(xq, xs, wq.reshape(d, n), ws.reshape(d, n // 64), threads=8)
+    assert np.array_equal(y[-1], (res[-1] + ref).astype(np.float32))
+
+
+def _mm(x_d, w_d, n, d, T, res=None):
+    y = torch.empty((T, d), dtype=torch.float32, device="cuda")
+    check(lib().leap_op_matmul(_s(), y.data_ptr(), x_d.data_ptr(), w_d.data_ptr(), n, d, T,
+                               res.data_ptr() if res is not None else None))
+    return y
+
+
+@pytest.mark.parametrize("n,d,T", [(2048, 256, 1), (2048, 5632, 1), (5632, 2048, 1),
+                                   (2048, 32000, 1), (2048, 2560, 7), (5632, 2048, 64),
+                                   (2048, 256, 130)])
+def test_matmul_f32(cuda, n, d, T):
+    r = np.random.default_rng(n + d + T)
+    x = r.standard_normal((T, n)).astype(np.float32)
+    w = (r.standard_normal((d, n)) * 0.02).astype(np.float32)
+    res = r.standard_normal((T, d)).astype(np.float32)
+    y = _mm(_dev(x), _dev(w), n, d, T, _dev(res)).cpu().numpy()
+    for t in sorted({0, T // 2, T - 1}):
+        ref = oracle.matmul(x[t], w, threads=8)
+        # both are FP32 sums of n products in different association orders:
+        # each is within ~sqrt(n) * eps * sum|w x| of the exact value
+        bound = 4 * np.sqrt(n) * np.finfo(np.float32).eps * (np.abs(w) @ np.abs(x[t]))
+        err = np.abs((y[t] - res[t]) - ref)
+        assert (err <= bound + 2 * np.finfo(np.float32).eps * np.abs(res[t])).all(), (
+            t, float(err.max()), float(bound.min()))
+
+
+@pytest.mark.parametrize("rows,dim", [(1, 2048), (1, 4096), (1, 8192), (37, 2048)])
+def test_rmsnorm(cuda, rows, dim):
+    r = np.random.default_rng(dim + rows)
+    x = (r.standard_normal((rows, dim)) * 4).astype(np.float32)
+    w = r.standard_normal(dim).astype(np.float32)
+    x_d = _dev(x)
+    o = torch.empty_like(x_d)
+    check(lib().leap_op_rmsnorm(_s(), o.data_ptr(), x_d.data_ptr(), _dev(w).data_ptr(), rows,
+                                dim))
+    # in place, as the head uses it
+    check(lib().leap_op_rmsnorm(_s(), x_d.data_ptr(), x_d.data_ptr(), _dev(w).data_ptr(), rows,
+                                dim))
+    o = o.cpu().numpy()
+    assert np.array_equal(o, x_d.cpu().numpy())
+    for i in sorted({0, rows - 1}):
+        ref = oracle.rmsnorm(x[i], w)
+        assert np.abs(o[i] - ref).max() <= 1e-6 * np.abs(ref).max()
+
+
+def _lane_order_argmax(v):
+    """The reference scan (Sampler.cpp:20-120) keeps one running maximum per
+    lane of 8 with a strict >, then reduces the lanes in order, and scans the
+    n % 8 tail last: ties go to the lowest lane, then the lowest index."""
+    n8 = v.size & ~7
+    best = max(range(v.size), key=lambda i: (v[i], -(i & 7 if i < n8 else 8), -i))
+    return best
+
+
+@pytest.mark.parametrize("n,ties", [(1, []), (7, [2, 5]), (32000, [9, 16]),
+                                    (32000, [15, 8, 31999]), (128256, [17, 90, 128255]),
+                                    (32003, [32001, 31999])])
+def test_argmax_reference_tie_order(cuda, n, ties):
+    r = np.random.default_rng(n + len(ties))
+    v = r.standard_normal(n).astype(np.float32)
+    if ties:
+        v[ties] = v.max() + 1
+    tok = torch.empty(1, dtype=torch.int32, device="cuda")
+    check(lib().leap_op_argmax(_s(), tok.data_ptr(), _dev(v).data_ptr(), n))
+    want = oracle.ref_argmax(v) if oracle.has_ref_engine() else _lane_order_argmax(v)
+    assert int(tok.item()) == want == _lane_order_argmax(v)
+
+
+def test_op_argument_errors(cuda):
+    x = torch.zeros(100, device="cuda")
+    q = torch.zeros(100, dtype=torch.int8, device="cuda")
+    with pytest.raises(LeapError):
+        check(lib().leap_op_quantize(_s(), q.data_ptr(), x.data_ptr(), x.data_ptr(), 100, 64))
+    with pytest.raises(LeapError):
+        check(lib().leap_op_qmatmul(_s(), x.data_ptr(), q.data_ptr(), x.data_ptr(), q.data_ptr(),
+                                    x.data_ptr(), 128, 1, 1, 32, None))
+    with pytest.raises(LeapError):
+        check(lib().leap_op_matmul(_s(), x.data_ptr(), x.data_ptr(), x.data_ptr(), 6, 1, 1, None))
