@@ -459,10 +459,242 @@ def run_prefill(args):
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------------------
+# End-to-end models (BASELINE configs 1 and 5, and the metric's 8B W8A8 shape)
+# ---------------------------------------------------------------------------
+
+# name: (dim, hidden, layers, heads, kv heads, vocab, seq_len), W8A8?, theta,
+#       prompt tokens, generated tokens
+MODELS = {
+    "tinyllama-fp32": ((2048, 5632, 22, 32, 4, 32000, 2048), False, 10000.0, 32, 256),
+    "llama3-8b-w8a8": ((4096, 14336, 32, 32, 8, 128256, 8448), True, 500000.0, 8192, 256),
+    "llama3-70b-w8a8": ((8192, 28672, 80, 64, 8, 128256, 8448), True, 500000.0, 8192, 256),
+}
+
+
+def model_bytes_per_token(shape, q8, ctx):
+    """Bytes one decode token must move: every weight once (int8 + one FP32
+    scale per 64, or FP32), the norms, and K/V rows 0..ctx of every layer."""
+    dim, hid, L, nh, nkv, vocab, _ = shape
+    kv = nkv * (dim // nh)
+    per_w = (1 + 4 / 64) if q8 else 4
+    layer_w = (dim * dim * 2 + 2 * kv * dim + 3 * hid * dim) * per_w + 2 * dim * 4
+    cls = vocab * dim * per_w + dim * 4
+    kv_bytes = L * 2 * kv * ctx * 4
+    return L * layer_w + cls + kv_bytes
+
+
+def run_model(args):
+    """Prefill a random prompt, then greedy-decode, through N pipeline stages
+    (N = the number of ranks; 1 = the single-GPU engine).  Synthetic
+    N(0, 0.02) weights (W8A8: quantized per group of 64) generated on the
+    device; RMSNorm weights 1.0.  Decode tok/s is timed from the first
+    generated token, as the reference's generate() does (main.cpp:100-107)."""
+    import torch
+    import torch.distributed as dist
+    from leap_b200 import ModelConfig, Transformer
+    from leap_b200.pipeline import PipelineStage, stage_range
+
+    shape, q8, theta, prompt_len, gen = MODELS[args.model]
+    prompt_len = args.prompt or prompt_len
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    cfg = ModelConfig(*shape)
+    lb, le = stage_range(cfg.n_layers, rank, world)
+    chunk = 512
+    eng = Transformer.synthetic(cfg, q8, seed=SEED, device=local, rope_theta=theta,
+                                layer_range=(lb, le), max_chunk=chunk)
+    eng.bind_torch_stream()
+    stage = PipelineStage(eng, cfg.dim, dev, max_chunk=chunk, rank=rank, world=world)
+    prompt = [int(t) for t in np.random.default_rng(SEED).integers(0, cfg.vocab_size,
+                                                                     prompt_len)]
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def timed(fn):
+        barrier()
+        torch.cuda.synchronize(dev)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        r = fn()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        eng.sync()
+        return r, max_over_ranks(e0.elapsed_time(e1) / 1e3)
+
+    # warm-up: a short prompt and a few tokens, then a clean cache
+    stage.prefill(prompt[:64], 0)
+    stage.decode(64, args.warmup)
+    torch.cuda.synchronize(dev)
+    eng.clear_kv_cache()
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    _, prefill_s = timed(lambda: stage.prefill(prompt, 0))
+    warm = args.warmup
+    steps = args.steps if args.steps_given else gen - 1 - warm
+    stage.decode(prompt_len, warm)  # untimed decode steps, positions continue
+    toks, decode_s = timed(lambda: stage.decode(prompt_len + warm, steps))
+    clocks = sampler.stop()
+    ctx_mid = prompt_len + warm + steps // 2
+    per_tok = model_bytes_per_token(shape, q8, ctx_mid)
+    tok_s = steps / decode_s
+    peak, peak_kind = load_peaks()
+
+    e2e = None
+    if world == 1 and not args.no_e2e:
+        # the reference-facing call: forward(token, pos) with the logits read
+        # back to the host every step (Transformer.h:56)
+        # positions re-used from the timed run (rows are rewritten; the
+        # attention work per token is the same)
+        nxt = int(toks[-1].item())
+        n_e2e = min(steps, 64)
+        pos = prompt_len + warm + steps - n_e2e
+        t0 = time.perf_counter()
+        for i in range(n_e2e):
+            eng.forward(nxt, pos + i)
+            nxt = eng.last_token
+        e2e_s = time.perf_counter() - t0
+        e2e = {"value": round(n_e2e / e2e_s, 2), "unit": "tok/s",
+               "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4 * cfg.vocab_size + 4,
+               "path": "Transformer.forward(token, pos) -> host logits, per token"}
+
+    line = None
+    if rank == 0:
+        # per token: embedding; per layer 12 kernels (W8A8: norm, quantize,
+        # qkv, attention, quantize, wo, norm, quantize, w13, silu, quantize, w2)
+        # or 8 (FP32); head: norm, [quantize], classifier, argmax
+        n_layers_launch = 1 + 12 * cfg.n_layers + 4 if q8 else 1 + 8 * cfg.n_layers + 3
+        line = {
+            "metric": f"decode tok/s ({args.model})", "value": round(tok_s, 2), "unit": "tok/s",
+            "n_gpus": world, "steps": steps, "warmup": warm,
+            "ms_per_step": round(decode_s / steps * 1e3, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "int8 x int8 -> f32" if q8
+            else "f32", "data": "synthetic (seeded N(0,0.02) weights on device, random ids)",
+            "config": {"workload": f"{args.model}: batch 1, {prompt_len}-token prompt prefilled, "
+                                   f"then greedy decode", "model": args.model,
+                       "global_batch": 1, "seq_len": prompt_len + warm + steps,
+                       "parallelism": f"pp{world}" if world > 1 else "single",
+                       "stages": [list(stage_range(cfg.n_layers, r, world))
+                                  for r in range(world)],
+                       "l2": f"inputs > L2: {per_tok / 1e9:.2f} GB of weights and KV per token"},
+            "prefill": {"tokens": prompt_len, "seconds": round(prefill_s, 3),
+                        "tok_s": round(prompt_len / prefill_s, 1)},
+            "roofline": {"bound": "hbm", "achieved": round(per_tok * tok_s / 1e9, 1),
+                         "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                         "frac": round(per_tok * tok_s / 1e9 / peak, 4),
+                         "bytes_per_token": int(per_tok), "traffic": None,
+                         "note": "whole decode step (all kernels) against one GPU's HBM; "
+                                 "stages run one after another for batch 1"},
+            "e2e": e2e,
+            "gpu_launches": n_layers_launch * steps,
+            "clocks": clocks,
+        }
+    eng.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = model_cpu_baseline(args.model, prompt_len + warm + steps // 2,
+                                                  args.cpu_seconds)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def run_model_reference(args):
+    """The reference engine's decode tok/s for --model on the host cores
+    (rank 0 only; other ranks exit without work)."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    shape, q8, theta, prompt_len, gen = MODELS[args.model]
+    prompt_len = args.prompt or prompt_len
+    cb = model_cpu_baseline(args.model, prompt_len + gen // 2, max(args.cpu_seconds, 5.0))
+    if cb is None:
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref was not built"}))
+        return
+    line = {"impl": "reference", "metric": f"decode tok/s ({args.model})",
+            "value": cb["value"], "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": cb["ms_per_token"], "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "int8 x int8 -> f32" if q8
+            else "f32", "data": "synthetic",
+            "config": {"workload": f"{args.model}: batch 1, decode at position "
+                                   f"{prompt_len + gen // 2}", "model": args.model},
+            "cpu_baseline": cb,
+            "e2e": {"value": cb["value"], "unit": "tok/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def model_cpu_baseline(name, ctx, seconds):
+    """The reference engine (oracle/_ref, Transformer::create + forward) on
+    this host: decode tok/s at position `ctx`.  Attention cost does not
+    depend on the cache contents, so forward(token, pos) is called at
+    pos = ctx.. directly.  Models too large for a bounded sample are timed on
+    1- and 3-layer files of the same shape and extrapolated linearly in the
+    layer count (labelled)."""
+    import oracle
+    from leap_b200.modelfile import ModelConfig, write_timing_file
+    if not oracle.has_ref_engine():
+        return None
+    shape, q8, theta, _, _ = MODELS[name]
+    threads = os.cpu_count() or 1
+    os.environ["OMP_NUM_THREADS"] = str(threads)
+    cfg = ModelConfig(*shape)
+    cfg.seq_len = max(cfg.seq_len, ctx + 64)
+    full = name == "tinyllama-fp32"
+    layer_counts = [cfg.n_layers] if full else [1, 3]
+    times = []
+    with tempfile.TemporaryDirectory() as d:
+        for nl in layer_counts:
+            c = ModelConfig(cfg.dim, cfg.hidden_dim, nl, cfg.n_heads, cfg.n_kv_heads,
+                            cfg.vocab_size, cfg.seq_len)
+            path = os.path.join(d, f"m{nl}.bin")
+            write_timing_file(path, c, q8)
+            ref = oracle.RefEngine(path, theta_10k=(theta == 10000.0))
+            ref.forward(1, ctx)  # warm-up (page-in of the mmapped weights)
+            n, t0 = 0, time.perf_counter()
+            while True:
+                ref.forward(1 + n, ctx + 1 + n)
+                n += 1
+                if time.perf_counter() - t0 >= seconds / len(layer_counts) or n >= 64:
+                    break
+            times.append((time.perf_counter() - t0) / n)
+            ref.close()
+            os.unlink(path)
+    if full:
+        sec = times[0]
+        sample = f"{len(layer_counts)} file: full model, forward() at pos {ctx}.."
+    else:
+        per_layer = (times[1] - times[0]) / 2
+        sec = times[0] + (cfg.n_layers - 1) * per_layer
+        sample = (f"extrapolated: 1- and 3-layer files of the same shape timed at pos {ctx}.., "
+                  f"{times[0] * 1e3:.1f} / {times[1] * 1e3:.1f} ms per token, "
+                  f"x{cfg.n_layers} layers")
+    return {"value": round(1 / sec, 3), "unit": "tok/s", "cores": threads,
+            "kind": "reference", "sample": sample, "ms_per_token": round(sec * 1e3, 2)}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["leap", "reference"], default="leap")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -479,11 +711,22 @@ def main():
                     help="0 tcgen05 3xTF32, 1 CUDA-core FP32")
     ap.add_argument("--layers", type=int, default=N_LAYERS)
     ap.add_argument("--ctx", type=int, default=CTX)
+    ap.add_argument("--model", choices=sorted(MODELS), default=None,
+                    help="end-to-end decode of a whole model (pipeline over the ranks)")
+    ap.add_argument("--prompt", type=int, default=0, help="prompt tokens for --model")
     args = ap.parse_args()
+    args.steps_given = args.steps is not None
+    if args.steps is None:
+        args.steps = 20
     if args.warmup < 3 and args.impl == "leap":
         args.warmup = 3  # timing rule: at least 3 warm-up steps
     if args.impl == "reference":
-        run_reference_arm(args)
+        if args.model:
+            run_model_reference(args)
+        else:
+            run_reference_arm(args)
+    elif args.model:
+        run_model(args)
     elif args.prefill:
         run_prefill(args)
     else:

@@ -300,6 +300,10 @@ LEAP_API int leap_engine_clear_kv(leap_engine *e);
 
 /* Stage operations on device buffers (asynchronous on the engine stream):
  *   embed:  x[n][dim] <- embedding rows of tokens[0..n) (host ints)
+ *   embed_device: the same from device ints (no host round trip, so a
+ *           pipeline's first stage can embed the token the last stage sent;
+ *           ids outside [0, vocab) read row 0 and set the engine's error,
+ *           reported by leap_engine_sync)
  *   layers: this engine's layers on x[n][dim] in place, for positions
  *           pos0..pos0+n-1 (n = 1 is the decode step; n > 1 a prompt chunk,
  *           n <= max_chunk)
@@ -307,6 +311,7 @@ LEAP_API int leap_engine_clear_kv(leap_engine *e);
  *           into logits[vocab] (device, or NULL) and the greedy token into
  *           *token (device int, or NULL). */
 LEAP_API int leap_engine_embed(leap_engine *e, const int *tokens, int n, float *x);
+LEAP_API int leap_engine_embed_device(leap_engine *e, const int *tokens_dev, int n, float *x);
 LEAP_API int leap_engine_layers(leap_engine *e, int pos0, int n, float *x);
 LEAP_API int leap_engine_head(leap_engine *e, float *x, float *logits, int *token);
 
@@ -335,6 +340,13 @@ LEAP_API int leap_set_prefill_impl(leap_ctx *ctx, int impl);
  * 1/sqrt(mean(x^2) + 1e-5).  o may equal x. */
 LEAP_API int leap_op_rmsnorm(void *stream, float *o, const float *x,
                              const float *w, int rows, int dim);
+/* rmsnorm followed by the activation quantize below, in one kernel (the
+ * W8A8 engine consumes the normalised row only quantized,
+ * QuantizedTransformer.cpp:925-951): q/s as leap_op_quantize with gs 64 of
+ * the rows leap_op_rmsnorm would produce.  dim % 64 == 0. */
+LEAP_API int leap_op_rmsnorm_quantize(void *stream, int8_t *q, float *s,
+                                      const float *x, const float *w,
+                                      int rows, int dim);
 /* Activation quantize (QuantizedTransformer.cpp:338-357): per group of gs,
  * s = max|x| * (1/127), q = round(x / s).  n % gs == 0. */
 LEAP_API int leap_op_quantize(void *stream, int8_t *q, float *s,

@@ -91,11 +91,14 @@ SIGNATURES: dict[str, tuple] = {
     "leap_engine_sync": (c_int, [c_void_p]),
     "leap_engine_clear_kv": (c_int, [c_void_p]),
     "leap_engine_embed": (c_int, [c_void_p, c_int_p, c_int, c_void_p]),
+    "leap_engine_embed_device": (c_int, [c_void_p, c_void_p, c_int, c_void_p]),
     "leap_engine_layers": (c_int, [c_void_p, c_int, c_int, c_void_p]),
     "leap_engine_head": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p]),
     "leap_engine_forward": (c_int, [c_void_p, c_int, c_int, c_float_p, c_int_p]),
     "leap_engine_prefill": (c_int, [c_void_p, c_int_p, c_int, c_int, c_int_p]),
     "leap_op_rmsnorm": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int]),
+    "leap_op_rmsnorm_quantize": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int,
+                                         c_int]),
     "leap_op_quantize": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, ctypes.c_longlong,
                                  c_int]),
     "leap_op_matmul": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,

@@ -90,7 +90,10 @@ int check_device_error(leap_ctx *c) {
     cudaMemset(c->d_err, 0, sizeof(int));
     for (int i = 0; i < 2; ++i)
         cudaMemset(c->counters[i], 0, sizeof(unsigned) * kMaxSeqPerLaunch * c->n_kv);
-    set_error("a kernel reported device error %d (bounded wait timed out)", err);
+    if (err == kDevErrBadToken)
+        set_error("a device-side token id was outside [0, vocab_size)");
+    else
+        set_error("a kernel reported device error %d (bounded wait timed out)", err);
     return LEAP_ERR_DEVICE;
 }
 

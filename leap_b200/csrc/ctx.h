@@ -67,6 +67,9 @@ namespace leap {
 
 constexpr int kMaxDevices = 64;
 
+// Device error word codes (bounded waits use small positive codes).
+constexpr int kDevErrBadToken = 0x70;  // a device-side token id outside [0, vocab)
+
 // thread-local last error
 void set_error(const char *fmt, ...);
 void clear_error();

@@ -464,18 +464,24 @@ int layers_one(leap_engine *e, int pos, float *x) {
     const leap_model_config &c = e->cfg;
     const int dim = c.dim, hid = c.hidden_dim, kv = e->kv_dim, gs = c.group_size;
     const bool q8 = c.quantized;
+    // W8A8: the normalised / activated vectors are only consumed quantized,
+    // so RMSNorm and SiLU*up write (q, s) directly (one kernel instead of two)
+    auto norm = [&](const float *w) {
+        return q8 ? rmsnorm_quantize(e->stream, e->aq, e->as, x, w, 1, dim)
+                  : rmsnorm(e->stream, e->xb, x, w, 1, dim);
+    };
     for (int i = 0; i < e->n_local; ++i) {
-        ETRY(rmsnorm(e->stream, e->xb, x, e->rms_att + size_t(i) * dim, 1, dim));
-        if (q8) ETRY(quantize(e->stream, e->aq, e->as, e->xb, dim, gs));
+        ETRY(norm(e->rms_att + size_t(i) * dim));
         ETRY(linear_vec(e, e->qkv, e->xb, e->wqkv[i], 0, dim + 2 * kv, nullptr));
         ETRY(leap_attn_decode(e->attn, i, pos, e->qkv, e->qkv + dim, e->qkv + dim + kv, e->att));
         if (q8) ETRY(quantize(e->stream, e->aq, e->as, e->att, dim, gs));
         ETRY(linear_vec(e, x, e->att, e->wo[i], 0, dim, x));  // x += wo . att
-        ETRY(rmsnorm(e->stream, e->xb, x, e->rms_ffn + size_t(i) * dim, 1, dim));
-        if (q8) ETRY(quantize(e->stream, e->aq, e->as, e->xb, dim, gs));
+        ETRY(norm(e->rms_ffn + size_t(i) * dim));
         ETRY(linear_vec(e, e->h13, e->xb, e->w13[i], 0, 2 * hid, nullptr));
-        ETRY(silu_mul(e->stream, e->h13, e->h13 + hid, hid));
-        if (q8) ETRY(quantize(e->stream, e->aq, e->as, e->h13, hid, gs));
+        if (q8)
+            ETRY(silu_mul_quantize(e->stream, e->aq, e->as, e->h13, e->h13 + hid, hid));
+        else
+            ETRY(silu_mul(e->stream, e->h13, e->h13 + hid, hid));
         ETRY(linear_vec(e, x, e->h13, e->w2[i], 0, dim, x));  // x += w2 . h
     }
     return LEAP_OK;
@@ -487,21 +493,25 @@ int layers_chunk(leap_engine *e, int pos0, int T, float *x) {
     const leap_model_config &c = e->cfg;
     const int dim = c.dim, hid = c.hidden_dim, kv = e->kv_dim, gs = c.group_size;
     const bool q8 = c.quantized;
+    auto norm = [&](const float *w) {
+        return q8 ? rmsnorm_quantize(e->stream, e->baq, e->bas, x, w, T, dim)
+                  : rmsnorm(e->stream, e->bxb, x, w, T, dim);
+    };
     for (int i = 0; i < e->n_local; ++i) {
-        ETRY(rmsnorm(e->stream, e->bxb, x, e->rms_att + size_t(i) * dim, T, dim));
-        if (q8) ETRY(quantize(e->stream, e->baq, e->bas, e->bxb, size_t(T) * dim, gs));
+        ETRY(norm(e->rms_att + size_t(i) * dim));
         ETRY(linear_mat(e, e->bq, e->bxb, e->wqkv[i], 0, dim, T, nullptr));
         ETRY(linear_mat(e, e->bk, e->bxb, e->wqkv[i], dim, kv, T, nullptr));
         ETRY(linear_mat(e, e->bv, e->bxb, e->wqkv[i], dim + kv, kv, T, nullptr));
         ETRY(leap_attn_prefill(e->attn, 0, i, pos0, T, e->bq, e->bk, e->bv, e->batt));
         if (q8) ETRY(quantize(e->stream, e->baq, e->bas, e->batt, size_t(T) * dim, gs));
         ETRY(linear_mat(e, x, e->batt, e->wo[i], 0, dim, T, x));
-        ETRY(rmsnorm(e->stream, e->bxb, x, e->rms_ffn + size_t(i) * dim, T, dim));
-        if (q8) ETRY(quantize(e->stream, e->baq, e->bas, e->bxb, size_t(T) * dim, gs));
+        ETRY(norm(e->rms_ffn + size_t(i) * dim));
         ETRY(linear_mat(e, e->bh1, e->bxb, e->w13[i], 0, hid, T, nullptr));
         ETRY(linear_mat(e, e->bh3, e->bxb, e->w13[i], hid, hid, T, nullptr));
-        ETRY(silu_mul(e->stream, e->bh1, e->bh3, size_t(T) * hid));
-        if (q8) ETRY(quantize(e->stream, e->baq, e->bas, e->bh1, size_t(T) * hid, gs));
+        if (q8)
+            ETRY(silu_mul_quantize(e->stream, e->baq, e->bas, e->bh1, e->bh3, size_t(T) * hid));
+        else
+            ETRY(silu_mul(e->stream, e->bh1, e->bh3, size_t(T) * hid));
         ETRY(linear_mat(e, x, e->bh1, e->w2[i], 0, dim, T, x));
     }
     return LEAP_OK;
@@ -509,8 +519,10 @@ int layers_chunk(leap_engine *e, int pos0, int T, float *x) {
 
 int head(leap_engine *e, float *x, float *logits, int *token) {
     const leap_model_config &c = e->cfg;
-    ETRY(rmsnorm(e->stream, x, x, e->rms_final, 1, c.dim));
-    if (c.quantized) ETRY(quantize(e->stream, e->aq, e->as, x, c.dim, c.group_size));
+    if (c.quantized)  // x is only consumed quantized (QuantizedTransformer.cpp:1056-1059)
+        ETRY(rmsnorm_quantize(e->stream, e->aq, e->as, x, e->rms_final, 1, c.dim));
+    else
+        ETRY(rmsnorm(e->stream, x, x, e->rms_final, 1, c.dim));
     float *lg = logits ? logits : e->logits;
     ETRY(linear_vec(e, lg, x, e->wcls, 0, c.vocab_size, nullptr));
     if (token) ETRY(argmax(e->stream, token, lg, c.vocab_size));
@@ -678,7 +690,22 @@ int leap_engine_embed(leap_engine *e, const int *tokens, int n, float *x) {
             "embed tokens"));
     }
     return embed(e->stream, x, e->emb.f, e->emb.q, e->emb.s, dtok, n, e->cfg.dim,
-                 e->cfg.group_size);
+                 e->cfg.group_size, e->cfg.vocab_size, e->attn->d_err);
+}
+
+int leap_engine_embed_device(leap_engine *e, const int *tokens_dev, int n, float *x) {
+    leap::clear_error();
+    if (!e || !tokens_dev || !x || n < 1 || n > e->max_chunk) {
+        leap::set_error("embed_device: bad arguments (n %d)", n);
+        return LEAP_ERR_INVALID;
+    }
+    if (!e->has_embed) {
+        leap::set_error("embed: this engine's layer range does not start at layer 0");
+        return LEAP_ERR_INVALID;
+    }
+    DevGuard g(e->device);
+    return embed(e->stream, x, e->emb.f, e->emb.q, e->emb.s, tokens_dev, n, e->cfg.dim,
+                 e->cfg.group_size, e->cfg.vocab_size, e->attn->d_err);
 }
 
 int leap_engine_layers(leap_engine *e, int pos0, int n, float *x) {
@@ -763,6 +790,16 @@ int leap_op_rmsnorm(void *stream, float *o, const float *x, const float *w, int 
         return LEAP_ERR_INVALID;
     }
     return rmsnorm(static_cast<cudaStream_t>(stream), o, x, w, rows, dim);
+}
+
+int leap_op_rmsnorm_quantize(void *stream, int8_t *q, float *s, const float *x, const float *w,
+                             int rows, int dim) {
+    leap::clear_error();
+    if (!q || !s || !x || !w || rows < 1 || dim < 64 || dim % 64) {
+        leap::set_error("rmsnorm_quantize: bad arguments (dim %d must be a multiple of 64)", dim);
+        return LEAP_ERR_INVALID;
+    }
+    return rmsnorm_quantize(static_cast<cudaStream_t>(stream), q, s, x, w, rows, dim);
 }
 
 int leap_op_quantize(void *stream, int8_t *q, float *s, const float *x, long long n, int gs) {

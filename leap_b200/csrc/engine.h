@@ -13,8 +13,10 @@ namespace leap {
 namespace eng {
 
 int embed(cudaStream_t st, float *x, const float *emb_f32, const int8_t *emb_q, const float *emb_s,
-          const int *tok_dev, int n, int dim, int gs);
+          const int *tok_dev, int n, int dim, int gs, int vocab, int *err);
 int rmsnorm(cudaStream_t st, float *o, const float *x, const float *w, int rows, int dim);
+int rmsnorm_quantize(cudaStream_t st, int8_t *q, float *s, const float *x, const float *w, int rows,
+                     int dim);
 int quantize(cudaStream_t st, int8_t *q, float *s, const float *x, size_t n, int gs);
 int gemv_q8(cudaStream_t st, float *y, const int8_t *xq, const float *xs, const int8_t *wq,
             const float *ws, int n, int d, const float *res);
@@ -25,6 +27,8 @@ int gemv_f32(cudaStream_t st, float *y, const float *x, const float *w, int n, i
 int gemm_f32(cudaStream_t st, float *y, const float *x, const float *w, int n, int d, int T,
              const float *res);
 int silu_mul(cudaStream_t st, float *h, const float *h3, size_t n);
+int silu_mul_quantize(cudaStream_t st, int8_t *q, float *s, const float *h, const float *h3,
+                      size_t n);
 int argmax(cudaStream_t st, int *out, const float *v, int n);
 int synth_normal(cudaStream_t st, float *w, size_t n, uint64_t seed, float std, float fill);
 

@@ -2,14 +2,23 @@
 // (src/inference/FloatTransformer.cpp:384-797 and
 // src/inference/QuantizedTransformer.cpp:654-1061), on the GPU.
 //
-// These are correct GPU versions, not the optimisation target: embedding
-// gather, RMSNorm, FP32 GEMV/GEMM, per-group activation quantization, the
-// W8A8 GEMV/GEMM, SiLU*up, residual adds, greedy argmax, and a synthetic
-// weight generator.  Two of them reproduce the reference's compiled
-// arithmetic bit for bit: the activation quantization (scale = max * (1/127),
-// round half away from zero) and the W8A8 dot (int32 group dots, then per
-// output val = fma(float(ival), w_s * x_s, val) over the groups in order).
+// Embedding gather, RMSNorm (optionally fused with the activation
+// quantization that follows it), FP32 GEMV/GEMM, per-group activation
+// quantization, the W8A8 GEMV/GEMM, SiLU*up (optionally fused with its
+// quantization), residual adds, greedy argmax, and a synthetic weight
+// generator.  Two reproduce the reference's compiled arithmetic bit for bit:
+// the activation quantization (scale = max * (1/127), id = 127/max, round
+// half away from zero) and the W8A8 dot (int32 group dots, then per output
+// val = fma(float(ival), w_s * x_s, val) over the groups in order).
+//
+// Batch-1 decode runs ~10 of these kernels per layer back to back, so the
+// decode-path kernels use programmatic dependent launch: each is launched
+// while its predecessor still runs, may read only constant data (weights)
+// before griddepcontrol.wait, and lets its own successor launch once it has
+// passed that wait.  The GEMVs use the window to start their weight stream.
 #include <cstdint>
+#include <mutex>
+#include <vector>
 
 #include "common.cuh"
 #include "engine.h"
@@ -24,35 +33,88 @@ __device__ __forceinline__ float warp_sum(float v) {
     return v;
 }
 
+__device__ __forceinline__ int4 ld_stream(const int4 *p) { return __ldcs(p); }
+__device__ __forceinline__ float4 ld_stream(const float4 *p) { return __ldcs(p); }
+
+// Programmatic dependent launch: wait for the predecessor kernel's results,
+// then allow the successor to start launching.
+__device__ __forceinline__ void pdl_enter() {
+    grid_dependency_wait();
+    grid_launch_dependents();
+}
+
+// One 64-value quantization group held as one float4 by each of 16
+// consecutive lanes (QuantizedTransformer.cpp:338-357 as compiled:
+// scale = max * (1/127), id = 127 / max, q = round half away (x * id)).
+// Every lane of the warp must call it (shuffles over the full warp).
+__device__ __forceinline__ void quantize16(float4 v, bool valid, char4 *q4, float *s, size_t i4) {
+    float mx = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+#pragma unroll
+    for (int o = 8; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const float inv127 = 1.0f / 127.0f;
+    const float scale = __fmul_rn(mx, inv127);
+    const float id = scale != 0.f ? __fdiv_rn(127.0f, mx) : 0.f;
+    if (!valid) return;
+    q4[i4] = make_char4(static_cast<signed char>(roundf(__fmul_rn(v.x, id))),
+                        static_cast<signed char>(roundf(__fmul_rn(v.y, id))),
+                        static_cast<signed char>(roundf(__fmul_rn(v.z, id))),
+                        static_cast<signed char>(roundf(__fmul_rn(v.w, id))));
+    if ((i4 & 15) == 0) s[i4 >> 4] = scale;
+}
+
 // ---- embedding -------------------------------------------------------------
 // FloatTransformer.cpp:758-759 (copy of the row); W8A8 engines dequantize the
-// table at load (QuantizedTransformer.cpp:116-117, :136-216): q * s.
+// table at load (QuantizedTransformer.cpp:116-117, :136-216): q * s.  Token
+// ids come from the device (a pipeline's last stage may have produced them):
+// an id outside [0, vocab) reads row 0 and raises the error word.
+__device__ __forceinline__ int checked_token(const int *tok, int row, int vocab, int *err) {
+    const int t = tok[row];
+    if (t >= 0 && t < vocab) return t;
+    if (threadIdx.x == 0) report_error(err, kDevErrBadToken);
+    return 0;
+}
+
 __global__ void embed_f32_kernel(float *__restrict__ x, const float *__restrict__ emb,
-                                 const int *__restrict__ tok, int dim) {
+                                 const int *__restrict__ tok, int dim, int vocab, int *err) {
+    pdl_enter();
     const int row = blockIdx.x;
-    const float *src = emb + size_t(tok[row]) * dim;
+    const float *src = emb + size_t(checked_token(tok, row, vocab, err)) * dim;
     for (int i = threadIdx.x; i < dim; i += blockDim.x) x[size_t(row) * dim + i] = src[i];
 }
 
 __global__ void embed_q8_kernel(float *__restrict__ x, const int8_t *__restrict__ q,
                                 const float *__restrict__ s, const int *__restrict__ tok,
-                                int dim, int gs) {
+                                int dim, int gs, int vocab, int *err) {
+    pdl_enter();
     const int row = blockIdx.x;
-    const size_t base = size_t(tok[row]) * dim;
+    const size_t base = size_t(checked_token(tok, row, vocab, err)) * dim;
     for (int i = threadIdx.x; i < dim; i += blockDim.x)
         x[size_t(row) * dim + i] = float(q[base + i]) * s[(base + i) / gs];
 }
 
-// ---- RMSNorm (FloatTransformer.cpp:79-214) ---------------------------------
+// ---- RMSNorm (FloatTransformer.cpp:79-214), optionally + quantize ----------
 // o = w * (r * x), r = 1/sqrt(mean(x^2) + 1e-5).  The reference's AVX2 path
 // refines an rsqrt estimate by one Newton step; 1/sqrtf is within 2e-7.
-__global__ void rmsnorm_kernel(float *o, const float *x,  // o may alias x
-                               const float *__restrict__ w, int dim) {
+// One CTA per row, one float4 per thread per pass.  QUANT: the normalised
+// row is quantized in groups of 64 (q, s) instead of being stored (the
+// W8A8 engine only consumes it quantized, QuantizedTransformer.cpp:925-951).
+template <bool QUANT>
+__global__ void __launch_bounds__(1024)
+rmsnorm_kernel(float *o, char4 *q4, float *s, const float *x,  // o may alias x
+               const float *__restrict__ w, int dim) {
+    pdl_enter();
     __shared__ float red[32];
-    const int row = blockIdx.x;
-    const float *xr = x + size_t(row) * dim;
+    const int row = blockIdx.x, n4 = dim >> 2;
+    const float4 *xr = reinterpret_cast<const float4 *>(x + size_t(row) * dim);
+    const float4 *w4 = reinterpret_cast<const float4 *>(w);
     float ss = 0.f;
-    for (int i = threadIdx.x; i < dim; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
+    for (int i = threadIdx.x; i < n4; i += blockDim.x) {
+        const float4 v = xr[i];
+        ss = fmaf(v.x, v.x, ss);
+        ss = fmaf(v.y, v.y, ss);
+        ss = fmaf(v.z, v.z, ss);
+        ss = fmaf(v.w, v.w, ss);
+    }
     ss = warp_sum(ss);
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
     __syncthreads();
@@ -65,14 +127,27 @@ __global__ void rmsnorm_kernel(float *o, const float *x,  // o may alias x
     float m = red[0] / float(dim);
     m += 1e-5f;
     const float r = 1.0f / sqrtf(m);
-    float *orow = o + size_t(row) * dim;
-    for (int i = threadIdx.x; i < dim; i += blockDim.x) orow[i] = w[i] * (r * xr[i]);
+    const int lim = (n4 + 31) & ~31;  // whole warps take part in the group shuffles
+    for (int i = threadIdx.x; i < lim; i += blockDim.x) {
+        const bool valid = i < n4;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (valid) {
+            const float4 xv = xr[i], wv = w4[i];
+            v = make_float4(wv.x * (r * xv.x), wv.y * (r * xv.y), wv.z * (r * xv.z),
+                            wv.w * (r * xv.w));
+        }
+        if (QUANT)
+            quantize16(v, valid, q4 + size_t(row) * n4, s + size_t(row) * (dim >> 6), size_t(i));
+        else if (valid)
+            reinterpret_cast<float4 *>(o + size_t(row) * dim)[i] = v;
+    }
 }
 
 // ---- activation quantization (QuantizedTransformer.cpp:338-357) ------------
-// One warp per group of `gs` (<= 128) values.
+// Any group size <= 128: one warp per group.
 __global__ void quantize_kernel(int8_t *__restrict__ q, float *__restrict__ s,
                                 const float *__restrict__ x, size_t n, int gs) {
+    pdl_enter();
     const size_t g = (size_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     const size_t i0 = g * gs;
@@ -91,63 +166,101 @@ __global__ void quantize_kernel(int8_t *__restrict__ q, float *__restrict__ s,
     for (int j = lane; j < cur; j += 32) q[i0 + j] = int8_t(roundf(__fmul_rn(x[i0 + j], id)));
 }
 
+// Group size 64: one float4 per thread, 16 lanes per group.
+__global__ void quantize64_kernel(char4 *__restrict__ q4, float *__restrict__ s,
+                                  const float *__restrict__ x, size_t n4) {
+    pdl_enter();
+    const size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x;  // grid covers whole warps
+    const bool valid = i < n4;
+    const float4 v = valid ? reinterpret_cast<const float4 *>(x)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    quantize16(v, valid, q4, s, i);
+}
+
 // ---- W8A8 GEMV (QuantizedTransformer.cpp:359-652) --------------------------
 // y[r] = (res ? res[r] : 0) + sum_g fma-chain(float(idot_g), ws[r,g]*xs[g]);
 // y may alias res (the residual add x += W.v), so neither is __restrict__.
-// A CTA takes 32 rows: phase 1 streams the int8 rows (16 bytes per thread,
-// coalesced), 4 threads reduce a 64-wide group's int32 dot; phase 2 runs
-// each row's group chain in order in one thread, as the reference does.
-constexpr int kQRows = 32;
-constexpr int kQThreads = 256;
+// A CTA takes kQR rows, two per warp.  Phase 1 streams the int8 rows with
+// kGemvUnroll 16-byte loads in flight per lane and row (the first batch is
+// issued before griddepcontrol.wait: weights do not depend on the previous
+// kernel); a 64-wide group is 4 consecutive chunks on 4 consecutive lanes,
+// whose dp4a partial dots meet by two xor-shuffles and go to shared memory
+// as float(int32 dot).  Phase 2 runs each row's chain over the groups in
+// order in one thread, as the reference's loop does.
+constexpr int kQR = 16;
+constexpr int kGemvWarps = 8;
+constexpr int kGemvUnroll = 8;
 
-__global__ void __launch_bounds__(kQThreads)
-gemv_q8_kernel(float *y, const int8_t *__restrict__ xq, const float *__restrict__ xs,
-               const int8_t *__restrict__ wq, const float *__restrict__ ws, int n, int d,
-               const float *res) {
-    extern __shared__ __align__(16) unsigned char sm[];
-    const int ngroups = n / 64;
-    const int ng1 = ngroups + 1;  // odd row stride: the per-row chains hit distinct banks
-    int8_t *sx = reinterpret_cast<int8_t *>(sm);                          // [n]
-    int *sdot = reinterpret_cast<int *>(sm + ((n + 15) & ~15));            // [kQRows][ng1]
-    float *sws = reinterpret_cast<float *>(sdot + kQRows * ng1);           // [kQRows][ng1]
-    float *sxs = sws + kQRows * ng1;                                       // [ngroups]
-    const int r0 = blockIdx.x * kQRows;
-    const int nrows = min(kQRows, d - r0);
-    for (int i = threadIdx.x * 16; i < n; i += kQThreads * 16)
-        *reinterpret_cast<int4 *>(sx + i) = *reinterpret_cast<const int4 *>(xq + i);
-    for (int i = threadIdx.x; i < nrows * ngroups; i += kQThreads) {
-        const int row = i / ngroups, g = i - row * ngroups;
-        sws[row * ng1 + g] = ws[size_t(r0) * ngroups + i];  // rows r0.. are contiguous
-    }
-    for (int g = threadIdx.x; g < ngroups; g += kQThreads) sxs[g] = xs[g];
-    __syncthreads();
-    const int chunks_per_row = n / 16;
-    const int total = nrows * chunks_per_row;
-    for (int f = threadIdx.x; f < kQRows * chunks_per_row; f += kQThreads) {
-        // every thread of a 4-lane group takes the same trip count: rows
-        // beyond d contribute zeros
+__device__ __forceinline__ void q8_group_dots(const int4 (&w)[kGemvUnroll], const int4 *sx, int nch,
+                                              int base, int lane, float *sdot_row) {
+#pragma unroll
+    for (int u = 0; u < kGemvUnroll; ++u) {
+        const int c = base + u * 32 + lane;
         int dot = 0;
-        const int row = f / chunks_per_row, ch = f - row * chunks_per_row;
-        if (f < total) {
-            const int4 w = *reinterpret_cast<const int4 *>(wq + size_t(r0 + row) * n + ch * 16);
-            const int4 xv = *reinterpret_cast<const int4 *>(sx + ch * 16);
-            dot = __dp4a(w.x, xv.x, dot);
-            dot = __dp4a(w.y, xv.y, dot);
-            dot = __dp4a(w.z, xv.z, dot);
-            dot = __dp4a(w.w, xv.w, dot);
+        if (c < nch) {
+            const int4 xv = sx[c];
+            dot = __dp4a(w[u].x, xv.x, dot);
+            dot = __dp4a(w[u].y, xv.y, dot);
+            dot = __dp4a(w[u].z, xv.z, dot);
+            dot = __dp4a(w[u].w, xv.w, dot);
         }
         dot += __shfl_xor_sync(0xffffffffu, dot, 1);
         dot += __shfl_xor_sync(0xffffffffu, dot, 2);
-        if ((ch & 3) == 0 && f < total) sdot[row * ng1 + (ch >> 2)] = dot;
+        if ((lane & 3) == 0 && c < nch) sdot_row[c >> 2] = float(dot);
+    }
+}
+
+__device__ __forceinline__ void q8_load(int4 (&w)[kGemvUnroll], const int4 *wr, bool row_ok, int nch,
+                                        int base, int lane) {
+#pragma unroll
+    for (int u = 0; u < kGemvUnroll; ++u) {
+        const int c = base + u * 32 + lane;
+        w[u] = (row_ok && c < nch) ? ld_stream(wr + c) : make_int4(0, 0, 0, 0);
+    }
+}
+
+__global__ void __launch_bounds__(kGemvWarps * 32)
+gemv_q8_kernel(float *y, const int8_t *__restrict__ xq, const float *__restrict__ xs,
+               const int8_t *__restrict__ wq, const float *__restrict__ ws, int n, int d,
+               const float *res) {
+    extern __shared__ int4 smx[];
+    const int nch = n >> 4, ng = n >> 6, ng1 = ng | 1;  // odd stride: phase 2 is conflict-free
+    int4 *sx = smx;                                      // [nch] x chunks
+    float *sxs = reinterpret_cast<float *>(sx + nch);    // [ng]
+    float *sdot = sxs + ng;                              // [kQR][ng1] float(int32 dot)
+    float *st = sdot + kQR * ng1;                        // [kQR][ng1] ws * xs
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int r0 = blockIdx.x * kQR;
+    const int ra = r0 + warp, rb = r0 + warp + kGemvWarps;
+    const bool oka = ra < d, okb = rb < d;
+    const int4 *wa = reinterpret_cast<const int4 *>(wq + size_t(oka ? ra : 0) * n);
+    const int4 *wb = reinterpret_cast<const int4 *>(wq + size_t(okb ? rb : 0) * n);
+    int4 pa[kGemvUnroll], pb[kGemvUnroll];
+    q8_load(pa, wa, oka, nch, 0, lane);
+    q8_load(pb, wb, okb, nch, 0, lane);
+    pdl_enter();
+    for (int i = threadIdx.x; i < nch; i += blockDim.x) sx[i] = reinterpret_cast<const int4 *>(xq)[i];
+    for (int g = threadIdx.x; g < ng; g += blockDim.x) sxs[g] = xs[g];
+    __syncthreads();
+    for (int i = threadIdx.x; i < kQR * ng; i += blockDim.x) {
+        const int rr = i / ng, g = i - rr * ng;
+        st[rr * ng1 + g] = (r0 + rr < d) ? __fmul_rn(ws[size_t(r0) * ng + i], sxs[g]) : 0.f;
+    }
+    for (int base = 0; base < nch; base += 32 * kGemvUnroll) {
+        if (base > 0) {
+            q8_load(pa, wa, oka, nch, base, lane);
+            q8_load(pb, wb, okb, nch, base, lane);
+        }
+        q8_group_dots(pa, sx, nch, base, lane, sdot + warp * ng1);
+        q8_group_dots(pb, sx, nch, base, lane, sdot + (warp + kGemvWarps) * ng1);
     }
     __syncthreads();
-    if (threadIdx.x < nrows) {
-        const int row = threadIdx.x;
+    if (threadIdx.x < kQR && r0 + threadIdx.x < d) {
+        const float *dr = sdot + threadIdx.x * ng1, *tr = st + threadIdx.x * ng1;
         float val = 0.f;
-#pragma unroll 4
-        for (int g = 0; g < ngroups; ++g)
-            val = fmaf(float(sdot[row * ng1 + g]), __fmul_rn(sws[row * ng1 + g], sxs[g]), val);
-        y[r0 + row] = res ? __fadd_rn(res[r0 + row], val) : val;
+#pragma unroll 8
+        for (int g = 0; g < ng; ++g) val = fmaf(dr[g], tr[g], val);
+        const int row = r0 + threadIdx.x;
+        y[row] = res ? __fadd_rn(res[row], val) : val;
     }
 }
 
@@ -231,25 +344,54 @@ gemm_q8_kernel(float *y, const int8_t *__restrict__ xq, const float *__restrict_
 }
 
 // ---- FP32 GEMV (FloatTransformer.cpp:240-382) ------------------------------
-// One warp per output row, float4 loads; y = (res ? res : 0) + W.x
-__global__ void __launch_bounds__(256)
+// One warp per row (grid-stride), kGemvUnroll float4 weight loads in flight
+// per lane, x in shared memory; y = (res ? res : 0) + W.x.  The first row's
+// first batch of weights is loaded before griddepcontrol.wait.
+__global__ void __launch_bounds__(kGemvWarps * 32)
 gemv_f32_kernel(float *y, const float *__restrict__ x, const float *__restrict__ w,
                 int n, int d, const float *res) {
-    const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+    extern __shared__ float4 sx4[];
+    const int n4 = n >> 2;
     const int lane = threadIdx.x & 31;
-    if (row >= d) return;
-    const float4 *wr = reinterpret_cast<const float4 *>(w + size_t(row) * n);
-    const float4 *xv = reinterpret_cast<const float4 *>(x);
-    float acc = 0.f;
-    for (int i = lane; i < n / 4; i += 32) {
-        const float4 a = wr[i], b = xv[i];
-        acc = fmaf(a.x, b.x, acc);
-        acc = fmaf(a.y, b.y, acc);
-        acc = fmaf(a.z, b.z, acc);
-        acc = fmaf(a.w, b.w, acc);
+    int row = blockIdx.x * kGemvWarps + (threadIdx.x >> 5);
+    float4 a[kGemvUnroll];
+    {
+        const float4 *wr = reinterpret_cast<const float4 *>(w + size_t(row < d ? row : 0) * n);
+#pragma unroll
+        for (int u = 0; u < kGemvUnroll; ++u) {
+            const int c = u * 32 + lane;
+            a[u] = (row < d && c < n4) ? ld_stream(wr + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
     }
-    acc = warp_sum(acc);
-    if (lane == 0) y[row] = res ? __fadd_rn(res[row], acc) : acc;
+    pdl_enter();
+    for (int i = threadIdx.x; i < n4; i += blockDim.x) sx4[i] = reinterpret_cast<const float4 *>(x)[i];
+    __syncthreads();
+    for (; row < d; row += gridDim.x * kGemvWarps) {
+        const float4 *wr = reinterpret_cast<const float4 *>(w + size_t(row) * n);
+        float acc = 0.f;
+        for (int base = 0; base < n4; base += 32 * kGemvUnroll) {
+            if (base > 0 || row != int(blockIdx.x * kGemvWarps + (threadIdx.x >> 5))) {
+#pragma unroll
+                for (int u = 0; u < kGemvUnroll; ++u) {
+                    const int c = base + u * 32 + lane;
+                    a[u] = c < n4 ? ld_stream(wr + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < kGemvUnroll; ++u) {
+                const int c = base + u * 32 + lane;
+                if (c < n4) {
+                    const float4 b = sx4[c];
+                    acc = fmaf(a[u].x, b.x, acc);
+                    acc = fmaf(a[u].y, b.y, acc);
+                    acc = fmaf(a[u].z, b.z, acc);
+                    acc = fmaf(a[u].w, b.w, acc);
+                }
+            }
+        }
+        acc = warp_sum(acc);
+        if (lane == 0) y[row] = res ? __fadd_rn(res[row], acc) : acc;
+    }
 }
 
 // ---- FP32 GEMM (prompt chunks): Y[t][r] = res + sum_k X[t][k] W[r][k] -------
@@ -296,14 +438,29 @@ gemm_f32_kernel(float *y, const float *__restrict__ x, const float *__restrict__
         }
 }
 
-// ---- SiLU(h1) * h3 (FloatTransformer.cpp:690-728) ---------------------------
-__global__ void silu_mul_kernel(float *__restrict__ h, const float *__restrict__ h3, size_t n) {
-    const size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (i < n) {
-        float v = h[i];
-        v = __fmul_rn(v, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-v))));
-        h[i] = __fmul_rn(v, h3[i]);
+// ---- SiLU(h1) * h3 (FloatTransformer.cpp:690-728), optionally + quantize --
+// (val * (1 / (1 + exp(-val)))) * h3 per element; QUANT quantizes the
+// result in groups of 64 (QuantizedTransformer.cpp:953-997) instead of
+// storing it.
+template <bool QUANT>
+__global__ void silu_mul_kernel(float *h, char4 *q4, float *s, const float *__restrict__ h3,
+                                size_t n4) {
+    pdl_enter();
+    const size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x;  // grid covers whole warps
+    const bool valid = i < n4;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (valid) {
+        const float4 a = reinterpret_cast<const float4 *>(h)[i];
+        const float4 b = reinterpret_cast<const float4 *>(h3)[i];
+        auto f = [](float t, float u) {
+            return __fmul_rn(__fmul_rn(t, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-t)))), u);
+        };
+        v = make_float4(f(a.x, b.x), f(a.y, b.y), f(a.z, b.z), f(a.w, b.w));
     }
+    if (QUANT)
+        quantize16(v, valid, q4, s, i);
+    else if (valid)
+        reinterpret_cast<float4 *>(h)[i] = v;
 }
 
 // ---- greedy argmax (Sampler.cpp:20-68) -------------------------------------
@@ -311,7 +468,7 @@ __global__ void silu_mul_kernel(float *__restrict__ h, const float *__restrict__
 // per lane), then takes lanes 0..7 in order with a strict '>', then the
 // tail past the last multiple of 8.  Equivalent total order used here:
 // larger value; then lane (i % 8, tail indices after every lane); then the
-// smaller index.
+// smaller index.  One CTA; each thread keeps 8 float4 loads in flight.
 __device__ __forceinline__ bool better(float v, int i, float bv, int bi, int n8) {
     if (v != bv) return v > bv;
     const int li = i < n8 ? (i & 7) : 8, lb = bi < n8 ? (bi & 7) : 8;
@@ -319,25 +476,47 @@ __device__ __forceinline__ bool better(float v, int i, float bv, int bi, int n8)
     return i < bi;
 }
 
-__global__ void argmax_kernel(int *__restrict__ out, const float *__restrict__ v, int n) {
+__device__ __forceinline__ void take(float v, int i, float &bv, int &bi, int n8) {
+    if (bi == 0x7fffffff || better(v, i, bv, bi, n8)) {
+        bv = v;
+        bi = i;
+    }
+}
+
+__global__ void __launch_bounds__(1024) argmax_kernel(int *__restrict__ out, const float *__restrict__ v, int n) {
+    pdl_enter();
     __shared__ float sv[32];
     __shared__ int si[32];
     const int n8 = n & ~7;
     float bv = -INFINITY;
     int bi = 0x7fffffff;
-    for (int i = threadIdx.x; i < n; i += blockDim.x)
-        if (bi == 0x7fffffff || better(v[i], i, bv, bi, n8)) {
-            bv = v[i];
-            bi = i;
+    const int n4 = ((reinterpret_cast<uintptr_t>(v) & 15) == 0) ? (n >> 2) : 0;
+    const float4 *v4 = reinterpret_cast<const float4 *>(v);
+    constexpr int U = 8;
+    for (int base = 0; base < n4; base += U * int(blockDim.x)) {
+        float4 a[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int j = base + u * int(blockDim.x) + int(threadIdx.x);
+            a[u] = j < n4 ? v4[j] : make_float4(0.f, 0.f, 0.f, 0.f);
         }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int j = base + u * int(blockDim.x) + int(threadIdx.x);
+            if (j < n4) {
+                take(a[u].x, 4 * j, bv, bi, n8);
+                take(a[u].y, 4 * j + 1, bv, bi, n8);
+                take(a[u].z, 4 * j + 2, bv, bi, n8);
+                take(a[u].w, 4 * j + 3, bv, bi, n8);
+            }
+        }
+    }
+    for (int i = 4 * n4 + threadIdx.x; i < n; i += blockDim.x) take(v[i], i, bv, bi, n8);
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) {
         const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
         const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (oi != 0x7fffffff && (bi == 0x7fffffff || better(ov, oi, bv, bi, n8))) {
-            bv = ov;
-            bi = oi;
-        }
+        if (oi != 0x7fffffff) take(ov, oi, bv, bi, n8);
     }
     if ((threadIdx.x & 31) == 0) {
         sv[threadIdx.x >> 5] = bv;
@@ -346,10 +525,7 @@ __global__ void argmax_kernel(int *__restrict__ out, const float *__restrict__ v
     __syncthreads();
     if (threadIdx.x == 0) {
         for (int w = 1; w < int(blockDim.x >> 5); ++w)
-            if (si[w] != 0x7fffffff && (si[0] == 0x7fffffff || better(sv[w], si[w], sv[0], si[0], n8))) {
-                sv[0] = sv[w];
-                si[0] = si[w];
-            }
+            if (si[w] != 0x7fffffff) take(sv[w], si[w], sv[0], si[0], n8);
         *out = si[0];
     }
 }
@@ -379,50 +555,136 @@ __global__ void synth_normal_kernel(float *__restrict__ w, size_t n, uint64_t se
 
 }  // namespace
 
+// Launch with programmatic stream serialization (the kernel calls
+// pdl_enter() before touching anything a previous kernel wrote).
+template <typename... KArgs, typename... Args>
+int launch_pdl(const char *what, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+               cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cuda_status(cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...), what);
+}
+
 int embed(cudaStream_t st, float *x, const float *emb_f32, const int8_t *emb_q, const float *emb_s,
-          const int *tok_dev, int n, int dim, int gs) {
+          const int *tok_dev, int n, int dim, int gs, int vocab, int *err) {
     if (emb_f32)
-        embed_f32_kernel<<<n, 256, 0, st>>>(x, emb_f32, tok_dev, dim);
-    else
-        embed_q8_kernel<<<n, 256, 0, st>>>(x, emb_q, emb_s, tok_dev, dim, gs);
-    return cuda_status(cudaGetLastError(), "embed");
+        return launch_pdl("embed", embed_f32_kernel, dim3(n), dim3(256), 0, st, x, emb_f32, tok_dev,
+                          dim, vocab, err);
+    return launch_pdl("embed", embed_q8_kernel, dim3(n), dim3(256), 0, st, x, emb_q, emb_s, tok_dev,
+                      dim, gs, vocab, err);
+}
+
+static unsigned row_threads(int dim) {
+    const int n4 = dim >> 2;
+    int t = ((n4 + 31) / 32) * 32;
+    return unsigned(t < 32 ? 32 : (t > 1024 ? 1024 : t));
 }
 
 int rmsnorm(cudaStream_t st, float *o, const float *x, const float *w, int rows, int dim) {
-    rmsnorm_kernel<<<rows, 256, 0, st>>>(o, x, w, dim);
-    return cuda_status(cudaGetLastError(), "rmsnorm");
+    if (dim % 4) {
+        set_error("rmsnorm: dim %d must be a multiple of 4", dim);
+        return LEAP_ERR_INVALID;
+    }
+    return launch_pdl("rmsnorm", rmsnorm_kernel<false>, dim3(rows), dim3(row_threads(dim)), 0, st, o,
+                      static_cast<char4 *>(nullptr), static_cast<float *>(nullptr), x, w, dim);
+}
+
+int rmsnorm_quantize(cudaStream_t st, int8_t *q, float *s, const float *x, const float *w, int rows,
+                     int dim) {
+    if (dim % 64) {
+        set_error("rmsnorm_quantize: dim %d must be a multiple of 64", dim);
+        return LEAP_ERR_INVALID;
+    }
+    return launch_pdl("rmsnorm_quantize", rmsnorm_kernel<true>, dim3(rows), dim3(row_threads(dim)),
+                      0, st, static_cast<float *>(nullptr), reinterpret_cast<char4 *>(q), s, x, w,
+                      dim);
 }
 
 int quantize(cudaStream_t st, int8_t *q, float *s, const float *x, size_t n, int gs) {
+    if (gs == 64 && n % 64 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+        (reinterpret_cast<uintptr_t>(q) & 3) == 0) {
+        const size_t n4 = n / 4, threads = 256;
+        const size_t blocks = (n4 + threads - 1) / threads;
+        return launch_pdl("quantize", quantize64_kernel, dim3(unsigned(blocks)), dim3(unsigned(threads)),
+                          0, st, reinterpret_cast<char4 *>(q), s, x, n4);
+    }
     const size_t groups = (n + gs - 1) / gs;
     const int threads = 256;
     const size_t blocks = (groups * 32 + threads - 1) / threads;
-    quantize_kernel<<<unsigned(blocks), threads, 0, st>>>(q, s, x, n, gs);
-    return cuda_status(cudaGetLastError(), "quantize");
+    return launch_pdl("quantize", quantize_kernel, dim3(unsigned(blocks)), dim3(threads), 0, st, q, s,
+                      x, n, gs);
 }
+
+// Grid for the warp-per-row FP32 GEMV: one warp per row, capped at the CTAs
+// the SMs hold at once, since each CTA stages x once and then walks rows
+// grid-stride.  Residency comes from
+// the occupancy calculator, cached per (device, kernel, shared memory).
+unsigned gemv_grid(const void *kernel, int items, size_t smem) {
+    struct Entry {
+        int dev;
+        const void *kernel;
+        size_t smem;
+        int ctas;
+    };
+    static std::mutex mu;
+    static std::vector<Entry> cache;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int ctas = 0;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        for (const Entry &e : cache)
+            if (e.dev == dev && e.kernel == kernel && e.smem == smem) ctas = e.ctas;
+        if (!ctas) {
+            int sms = 0, per_sm = 0;
+            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kGemvWarps * 32, smem);
+            ctas = (sms > 0 ? sms : 148) * (per_sm > 0 ? per_sm : 1);
+            cache.push_back({dev, kernel, smem, ctas});
+        }
+    }
+    const int want = (items + kGemvWarps - 1) / kGemvWarps;
+    return unsigned(want < ctas ? want : ctas);
+}
+
+int set_smem_attr(const void *fn, bool *done, size_t bytes, const char *what) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (done[dev]) return LEAP_OK;
+    const cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               int(bytes));
+    if (e != cudaSuccess) return cuda_status(e, what);
+    done[dev] = true;
+    return LEAP_OK;
+}
+
+constexpr size_t kGemvSmemMax = 200 * 1024;
 
 int gemv_q8(cudaStream_t st, float *y, const int8_t *xq, const float *xs, const int8_t *wq,
             const float *ws, int n, int d, const float *res) {
-    const size_t ng1 = size_t(n / 64) + 1;
-    const size_t smem = ((n + 15) & ~15) + 2 * kQRows * ng1 * 4 + size_t(n / 64) * 4;
     if (n % 64 != 0) {
         set_error("gemv_q8: n %d is not a multiple of 64", n);
         return LEAP_ERR_INVALID;
     }
-    // x and the per-row partials live in shared memory; beyond ~40k columns the
-    // tiled kernel (same accumulation order) takes over.
-    if (smem > 200 * 1024) return gemm_q8(st, y, xq, xs, wq, ws, n, d, 1, res);
+    const size_t ng = size_t(n / 64), ng1 = ng | 1;
+    const size_t smem = size_t(n) + ng * 4 + 2 * kQR * ng1 * 4;
+    // x, its scales and the per-row group dots live in shared memory; beyond
+    // that the tiled kernel (same accumulation order) takes over
+    if (smem > kGemvSmemMax) return gemm_q8(st, y, xq, xs, wq, ws, n, d, 1, res);
     static bool attr[kMaxDevices] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (!attr[dev]) {
-        const cudaError_t e = cudaFuncSetAttribute(
-            gemv_q8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(gemv_q8)");
-        attr[dev] = true;
-    }
-    gemv_q8_kernel<<<(d + kQRows - 1) / kQRows, kQThreads, smem, st>>>(y, xq, xs, wq, ws, n, d, res);
-    return cuda_status(cudaGetLastError(), "gemv_q8");
+    const int r = set_smem_attr(reinterpret_cast<const void *>(gemv_q8_kernel), attr, kGemvSmemMax,
+                                "cudaFuncSetAttribute(gemv_q8)");
+    if (r != LEAP_OK) return r;
+    return launch_pdl("gemv_q8", gemv_q8_kernel, dim3(unsigned((d + kQR - 1) / kQR)),
+                      dim3(kGemvWarps * 32), smem, st, y, xq, xs, wq, ws, n, d, res);
 }
 
 int gemm_q8(cudaStream_t st, float *y, const int8_t *xq, const float *xs, const int8_t *wq,
@@ -434,8 +696,19 @@ int gemm_q8(cudaStream_t st, float *y, const int8_t *xq, const float *xs, const 
 
 int gemv_f32(cudaStream_t st, float *y, const float *x, const float *w, int n, int d,
              const float *res) {
-    gemv_f32_kernel<<<(d + 7) / 8, 256, 0, st>>>(y, x, w, n, d, res);
-    return cuda_status(cudaGetLastError(), "gemv_f32");
+    const size_t smem = size_t(n) * 4;
+    if (n % 4 != 0) {
+        set_error("gemv_f32: n %d is not a multiple of 4", n);
+        return LEAP_ERR_INVALID;
+    }
+    if (smem > kGemvSmemMax) return gemm_f32(st, y, x, w, n, d, 1, res);
+    static bool attr[kMaxDevices] = {};
+    const int r = set_smem_attr(reinterpret_cast<const void *>(gemv_f32_kernel), attr, kGemvSmemMax,
+                                "cudaFuncSetAttribute(gemv_f32)");
+    if (r != LEAP_OK) return r;
+    const unsigned grid = gemv_grid(reinterpret_cast<const void *>(gemv_f32_kernel), d, smem);
+    return launch_pdl("gemv_f32", gemv_f32_kernel, dim3(grid), dim3(kGemvWarps * 32), smem,
+                      st, y, x, w, n, d, res);
 }
 
 int gemm_f32(cudaStream_t st, float *y, const float *x, const float *w, int n, int d, int T,
@@ -446,13 +719,28 @@ int gemm_f32(cudaStream_t st, float *y, const float *x, const float *w, int n, i
 }
 
 int silu_mul(cudaStream_t st, float *h, const float *h3, size_t n) {
-    silu_mul_kernel<<<unsigned((n + 255) / 256), 256, 0, st>>>(h, h3, n);
-    return cuda_status(cudaGetLastError(), "silu_mul");
+    if (n % 4) {
+        set_error("silu_mul: n must be a multiple of 4");
+        return LEAP_ERR_INVALID;
+    }
+    const size_t n4 = n / 4, blocks = (n4 + 255) / 256;
+    return launch_pdl("silu_mul", silu_mul_kernel<false>, dim3(unsigned(blocks)), dim3(256), 0, st,
+                      h, static_cast<char4 *>(nullptr), static_cast<float *>(nullptr), h3, n4);
+}
+
+int silu_mul_quantize(cudaStream_t st, int8_t *q, float *s, const float *h, const float *h3,
+                      size_t n) {
+    if (n % 64) {
+        set_error("silu_mul_quantize: n must be a multiple of 64");
+        return LEAP_ERR_INVALID;
+    }
+    const size_t n4 = n / 4, blocks = (n4 + 255) / 256;
+    return launch_pdl("silu_mul_quantize", silu_mul_kernel<true>, dim3(unsigned(blocks)), dim3(256),
+                      0, st, const_cast<float *>(h), reinterpret_cast<char4 *>(q), s, h3, n4);
 }
 
 int argmax(cudaStream_t st, int *out, const float *v, int n) {
-    argmax_kernel<<<1, 1024, 0, st>>>(out, v, n);
-    return cuda_status(cudaGetLastError(), "argmax");
+    return launch_pdl("argmax", argmax_kernel, dim3(1), dim3(1024), 0, st, out, v, n);
 }
 
 int synth_normal(cudaStream_t st, float *w, size_t n, uint64_t seed, float std, float fill) {

@@ -160,6 +160,11 @@ class Transformer:
         check(lib().leap_engine_embed(self.handle, t.ctypes.data_as(_ip), int(t.size),
                                       x.data_ptr()))
 
+    def embed_device(self, tokens, x) -> None:
+        """Embed int32 token ids that are already on the device."""
+        check(lib().leap_engine_embed_device(self.handle, tokens.data_ptr(), int(tokens.numel()),
+                                             x.data_ptr()))
+
     def layers(self, pos0: int, x) -> None:
         check(lib().leap_engine_layers(self.handle, pos0, int(x.shape[0]), x.data_ptr()))
 

@@ -140,3 +140,40 @@ def write_v2(path: str, cfg: ModelConfig, seed: int = 0, group_size: int = 64) -
             q, s = quantize_q80(_normal(seed, name, shape).reshape(-1), group_size)
             f.write(q.tobytes())
             f.write(s.tobytes())
+
+
+def write_timing_file(path: str, cfg: ModelConfig, quantized: bool, group_size: int = 64,
+                      seed: int = 0) -> None:
+    """A model file of `cfg`'s shape for TIMING only: every tensor is filled
+    from one repeated 16 MB block of N(0, 0.02) values (W8A8: their int8
+    codes and scales), which writes multi-GB files in seconds.  The engines'
+    work per token does not depend on the weight values."""
+    rng = np.random.default_rng(seed)
+    block = (rng.standard_normal(1 << 22, dtype=np.float32) * np.float32(0.02))
+    bq, bs = quantize_q80(block, group_size)
+
+    def fill(f, numel, kind):
+        src = {"f32": block, "q": bq, "s": bs}[kind]
+        while numel > 0:
+            n = min(numel, src.size)
+            f.write(src[:n].tobytes())
+            numel -= n
+
+    with open(path, "wb") as f:
+        if quantized:
+            hdr = (struct.pack("<Ii", MAGIC, 2) + struct.pack("<7i", *cfg.as_tuple()) + bytes([1])
+                   + struct.pack("<i", group_size))
+        else:
+            hdr = struct.pack("<Ii", MAGIC, 1) + struct.pack("<7i", *cfg.as_tuple()) + bytes([1])
+        f.write(hdr + bytes(256 - len(hdr)))
+        ones = np.ones(cfg.dim, np.float32).tobytes()
+        for _ in range(2 * cfg.n_layers + 1):
+            f.write(ones)
+        shapes = [("tok", (cfg.vocab_size, cfg.dim))] + _tensors(cfg, seed)
+        for name, shape in shapes:
+            numel = int(np.prod(shape))
+            if quantized:
+                fill(f, numel, "q")
+                fill(f, numel // group_size, "s")
+            else:
+                fill(f, numel, "f32")

@@ -142,6 +142,30 @@ def test_rmsnorm(cuda, rows, dim):
         assert np.abs(o[i] - ref).max() <= 1e-6 * np.abs(ref).max()
 
 
+@pytest.mark.parametrize("rows,dim", [(1, 2048), (1, 4096), (1, 8192), (9, 4096), (3, 14336 // 4)])
+def test_rmsnorm_quantize_equals_rmsnorm_then_quantize(cuda, rows, dim):
+    if dim % 64:
+        pytest.skip("W8A8 rows are multiples of 64")
+    r = np.random.default_rng(rows * dim)
+    x = (r.standard_normal((rows, dim)) * 3).astype(np.float32)
+    w = (1 + 0.1 * r.standard_normal(dim)).astype(np.float32)
+    x_d, w_d = _dev(x), _dev(w)
+    o = torch.empty_like(x_d)
+    check(lib().leap_op_rmsnorm(_s(), o.data_ptr(), x_d.data_ptr(), w_d.data_ptr(), rows, dim))
+    q1, s1 = _quantize_dev(o.reshape(-1))
+    q2 = torch.empty(rows * dim, dtype=torch.int8, device="cuda")
+    s2 = torch.empty(rows * dim // 64, dtype=torch.float32, device="cuda")
+    check(lib().leap_op_rmsnorm_quantize(_s(), q2.data_ptr(), s2.data_ptr(), x_d.data_ptr(),
+                                         w_d.data_ptr(), rows, dim))
+    torch.cuda.synchronize()
+    assert torch.equal(q1, q2)
+    assert torch.equal(s1.view(torch.int32), s2.view(torch.int32))
+    # and the quantization of the oracle's rmsnorm agrees but for last-bit
+    # rounding of the norm (codes within 1)
+    q0, _ = oracle.quantize(oracle.rmsnorm(x[0], w))
+    assert np.abs(q0.astype(int) - q2.cpu().numpy()[:dim].astype(int)).max() <= 1
+
+
 def _lane_order_argmax(v):
     """The reference scan (Sampler.cpp:20-120) keeps one running maximum per
     lane of 8 with a strict >, then reduces the lanes in order, and scans the
