@@ -106,6 +106,7 @@ SIGNATURES: dict[str, tuple] = {
     "leap_op_qmatmul": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                 c_int, c_int, c_int, c_int, c_void_p]),
     "leap_op_argmax": (c_int, [c_void_p, c_void_p, c_void_p, c_int]),
+    "leap_op_set_q8_gemv": (c_int, [c_int]),
 }
 
 _lock = threading.Lock()

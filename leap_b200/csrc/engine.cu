@@ -447,7 +447,7 @@ int linear_vec(leap_engine *e, float *y, const float *x, const Mat &w, int row0,
     const int n = w.cols;
     if (w.f) return gemv_f32(e->stream, y, x, w.f + size_t(row0) * n, n, rows, res);
     return gemv_q8(e->stream, y, e->aq, e->as, w.q + size_t(row0) * n,
-                   w.s + size_t(row0) * n / e->cfg.group_size, n, rows, res);
+                   w.s + size_t(row0) * n / e->cfg.group_size, n, rows, res, e->attn->d_err);
 }
 
 int linear_mat(leap_engine *e, float *y, const float *x, const Mat &w, int row0, int rows, int T,
@@ -833,6 +833,16 @@ int leap_op_qmatmul(void *stream, float *y, const int8_t *xq, const float *xs, c
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
     return T == 1 ? gemv_q8(st, y, xq, xs, wq, ws, n, d, res)
                   : gemm_q8(st, y, xq, xs, wq, ws, n, d, T, res);
+}
+
+int leap_op_set_q8_gemv(int impl) {
+    leap::clear_error();
+    if (impl != 0 && impl != 1) {
+        leap::set_error("q8 gemv impl %d (0 sliced, 1 register-staged)", impl);
+        return LEAP_ERR_INVALID;
+    }
+    leap::eng::g_q8_slice = impl == 0;
+    return LEAP_OK;
 }
 
 int leap_op_argmax(void *stream, int *token, const float *v, int n) {

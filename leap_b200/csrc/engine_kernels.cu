@@ -264,6 +264,83 @@ gemv_q8_kernel(float *y, const int8_t *__restrict__ xq, const float *__restrict_
     }
 }
 
+// ---- W8A8 GEMV, one row per lane ------------------------------------------
+// The same arithmetic as gemv_q8_kernel.  A CTA takes kSR rows; its 8 warps
+// split each row's groups into kSK contiguous slices (two per warp: lanes
+// 0..15 and 16..31), so lane (row r, slice k) computes the int32 dots of
+// row r's groups in slice k by itself — 16 dp4a over 4 chunks per group, no
+// shuffles — with kSU 16-byte loads in flight, and writes float(dot) and
+// ws*xs into a [row][group] table in shared memory.  Then kSR lanes run the
+// rows' chains over all groups, in order.  The first loads are issued
+// before griddepcontrol.wait.  (Measured end to end on the 8B decode step,
+// this beats both a persistent variant of it and the register-staged
+// kernel: its 64 registers let 4 CTAs per SM start their weight stream
+// while the previous kernel still runs.)
+constexpr int kSR = 16;   // rows per CTA
+constexpr int kSK = 16;   // slices of a row's groups per CTA (2 per warp)
+constexpr int kSU = 8;    // chunks (16 bytes) in flight per lane
+
+__global__ void __launch_bounds__(256, 4)
+gemv_q8_slice_kernel(float *y, const int8_t *__restrict__ xq, const float *__restrict__ xs,
+                     const int8_t *__restrict__ wq, const float *__restrict__ ws, int n, int d,
+                     const float *res) {
+    extern __shared__ int4 ssm[];
+    const int nch = n >> 4, ng = n >> 6, ng1 = ng | 1;
+    int4 *sx = ssm;                                     // [nch]
+    float *sxs = reinterpret_cast<float *>(sx + nch);   // [ng]
+    float *tdot = sxs + ng;                             // [kSR][ng1]
+    float *tt = tdot + kSR * ng1;                       // [kSR][ng1]
+    const int tid = threadIdx.x, lane = tid & 31;
+    const int rr = lane & (kSR - 1), k = (tid >> 5) * 2 + (lane >> 4);
+    const int row = blockIdx.x * kSR + rr;
+    const bool ok = row < d;
+    const int g0 = k * ng / kSK, g1 = (k + 1) * ng / kSK;  // this lane's groups
+    const int c0 = 4 * g0, c1 = 4 * g1;                     // and chunks
+    const int4 *wr = reinterpret_cast<const int4 *>(wq + size_t(ok ? row : 0) * n);
+    const float *wsr = ws + size_t(ok ? row : 0) * ng;
+    int4 w[kSU];
+#pragma unroll
+    for (int u = 0; u < kSU; ++u) w[u] = (ok && c0 + u < c1) ? __ldg(wr + c0 + u) : make_int4(0, 0, 0, 0);
+    pdl_enter();
+    for (int i = tid; i < nch; i += blockDim.x) sx[i] = reinterpret_cast<const int4 *>(xq)[i];
+    for (int g = tid; g < ng; g += blockDim.x) sxs[g] = xs[g];
+    __syncthreads();
+    for (int cb = c0; cb < c1; cb += kSU) {  // kSU % 4 == 0: whole groups per batch
+        if (cb > c0) {
+#pragma unroll
+            for (int u = 0; u < kSU; ++u)
+                w[u] = (ok && cb + u < c1) ? __ldg(wr + cb + u) : make_int4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int q = 0; q < kSU / 4; ++q) {
+            const int g = (cb >> 2) + q;
+            if (g < g1) {
+                int dot = 0;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int4 xv = sx[4 * g + j];
+                    const int4 wv = w[4 * q + j];
+                    dot = __dp4a(wv.x, xv.x, dot);
+                    dot = __dp4a(wv.y, xv.y, dot);
+                    dot = __dp4a(wv.z, xv.z, dot);
+                    dot = __dp4a(wv.w, xv.w, dot);
+                }
+                tdot[rr * ng1 + g] = float(dot);
+                tt[rr * ng1 + g] = ok ? __fmul_rn(__ldg(wsr + g), sxs[g]) : 0.f;
+            }
+        }
+    }
+    __syncthreads();
+    if (tid < kSR && blockIdx.x * kSR + tid < d) {
+        const float *dr = tdot + tid * ng1, *tr = tt + tid * ng1;
+        float val = 0.f;
+#pragma unroll 8
+        for (int g = 0; g < ng; ++g) val = fmaf(dr[g], tr[g], val);
+        const int r = blockIdx.x * kSR + tid;
+        y[r] = res ? __fadd_rn(res[r], val) : val;
+    }
+}
+
 // ---- W8A8 GEMM (prompt chunks): 64 rows x 32 tokens per CTA ---------------
 // Same per-(row, token) arithmetic as the GEMV: the int32 dot of each group,
 // then the ordered fma chain over groups.
@@ -668,8 +745,20 @@ int set_smem_attr(const void *fn, bool *done, size_t bytes, const char *what) {
 
 constexpr size_t kGemvSmemMax = 200 * 1024;
 
+bool g_q8_slice = true;
+
+int gemv_q8_slice(cudaStream_t st, float *y, const int8_t *xq, const float *xs, const int8_t *wq,
+                  const float *ws, int n, int d, const float *res, size_t smem) {
+    static bool attr[kMaxDevices] = {};
+    const int r = set_smem_attr(reinterpret_cast<const void *>(gemv_q8_slice_kernel), attr,
+                                kGemvSmemMax, "cudaFuncSetAttribute(gemv_q8_slice)");
+    if (r != LEAP_OK) return r;
+    return launch_pdl("gemv_q8_slice", gemv_q8_slice_kernel, dim3(unsigned((d + kSR - 1) / kSR)),
+                      dim3(256), smem, st, y, xq, xs, wq, ws, n, d, res);
+}
+
 int gemv_q8(cudaStream_t st, float *y, const int8_t *xq, const float *xs, const int8_t *wq,
-            const float *ws, int n, int d, const float *res) {
+            const float *ws, int n, int d, const float *res, int *err) {
     if (n % 64 != 0) {
         set_error("gemv_q8: n %d is not a multiple of 64", n);
         return LEAP_ERR_INVALID;
@@ -679,6 +768,7 @@ int gemv_q8(cudaStream_t st, float *y, const int8_t *xq, const float *xs, const 
     // x, its scales and the per-row group dots live in shared memory; beyond
     // that the tiled kernel (same accumulation order) takes over
     if (smem > kGemvSmemMax) return gemm_q8(st, y, xq, xs, wq, ws, n, d, 1, res);
+    if (g_q8_slice) return gemv_q8_slice(st, y, xq, xs, wq, ws, n, d, res, smem);
     static bool attr[kMaxDevices] = {};
     const int r = set_smem_attr(reinterpret_cast<const void *>(gemv_q8_kernel), attr, kGemvSmemMax,
                                 "cudaFuncSetAttribute(gemv_q8)");

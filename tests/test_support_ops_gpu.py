@@ -59,9 +59,17 @@ def _qmm(xq, xs, wq, ws, n, d, T, res=None):
     return y
 
 
+@pytest.fixture(params=[0, 1], ids=["sliced", "regs"])
+def q8_gemv(request):
+    check(lib().leap_op_set_q8_gemv(request.param))
+    yield request.param
+    check(lib().leap_op_set_q8_gemv(0))
+
+
 @pytest.mark.parametrize("n,d", [(2048, 256), (4096, 6144), (14336, 4096), (8192, 1024),
-                                 (28672, 256), (65536, 64)])
-def test_qmatmul_gemv_bit_exact(cuda, n, d):
+                                 (28672, 256), (65536, 64), (5632, 37), (4096, 3), (256, 9),
+                                 (4160, 100)])
+def test_qmatmul_gemv_bit_exact(cuda, q8_gemv, n, d):
     r = np.random.default_rng(n * 7 + d)
     x = r.standard_normal(n).astype(np.float32)
     w = (r.standard_normal((d, n)) * 0.02).astype(np.float32)
@@ -72,6 +80,13 @@ def test_qmatmul_gemv_bit_exact(cuda, n, d):
     xq, xs = oracle.quantize(x)
     ref = oracle.qmatmul(xq, xs, wq.reshape(d, n), ws.reshape(d, n // 64), threads=8)
     assert np.array_equal(y.cpu().numpy()[0], ref)
+    # with a residual, as the engine's x += W.v uses it (y aliases res)
+    res = _dev(np.arange(d, dtype=np.float32))
+    wq_d, ws_d = _dev(wq), _dev(ws)  # kept alive until the kernel has run
+    check(lib().leap_op_qmatmul(_s(), res.data_ptr(), xq_d.data_ptr(), xs_d.data_ptr(),
+                                wq_d.data_ptr(), ws_d.data_ptr(), n, d, 1, 64, res.data_ptr()))
+    torch.cuda.synchronize()
+    assert np.array_equal(res.cpu().numpy(), (np.arange(d, dtype=np.float32) + ref))
 
 
 @pytest.mark.parametrize("T", [2, 33, 100])
