@@ -127,7 +127,10 @@ LEAP_API int leap_set_overlap(leap_ctx *ctx, int enable);
  *       split-KV kernel (128-thread CTAs, two per SM) whose last CTA per
  *       (sequence, kv head) combines the partials;
  *   1 = that split-KV kernel;  2 = cluster kernel;
- *   3 = split-KV kernel with 256-thread CTAs, one per SM.
+ *   3 = split-KV kernel with 256-thread CTAs, one per SM;
+ *   4 = the split-KV kernel of 1 publishing its partials only, combined by a
+ *       second launch (one CTA per query head) that starts under
+ *       programmatic dependent launch.
  */
 LEAP_API int leap_set_decode_impl(leap_ctx *ctx, int impl);
 

@@ -282,7 +282,7 @@ int leap_ctx_use_own_stream(leap_ctx *c) {
 int leap_set_decode_impl(leap_ctx *c, int impl) {
     leap::clear_error();
     LEAP_CHECK_CTX(c);
-    if (impl < 0 || impl > 3) {
+    if (impl < 0 || impl > 4) {
         leap::set_error("decode impl %d unknown", impl);
         return LEAP_ERR_INVALID;
     }

@@ -77,7 +77,10 @@ struct DecodeArgs {
     float scale_log2;    // log2(e) / sqrt(HD)
 };
 
-template <int HD, int G, int NT>
+// TAIL: the last CTA of a (sequence, kv head) combines its splits (ticket);
+// otherwise every CTA only publishes its partial and decode_combine_kernel,
+// launched right after, combines them.
+template <int HD, int G, int NT, bool TAIL>
 __global__ void __launch_bounds__(NT, 256 / NT)
 decode_attn_kernel(const DecodeArgs a, const DecodeSeq tab) {
     using C = Cfg<HD, G, NT>;
@@ -355,6 +358,7 @@ decode_attn_kernel(const DecodeArgs a, const DecodeSeq tab) {
         a.part_ml[size_t(pidx) * C::MLS + 2 * tid + 0] = s_M[tid];
         a.part_ml[size_t(pidx) * C::MLS + 2 * tid + 1] = s_L[tid];
     }
+    if (!TAIL) return;  // decode_combine_kernel takes it from here
     __syncthreads();
     if (tid == 0) {
         // publish this CTA's partial (release, cumulative over the CTA's
@@ -451,17 +455,106 @@ decode_attn_kernel(const DecodeArgs a, const DecodeSeq tab) {
     }
 }
 
+// Split-KV combine as its own launch: one CTA of 4 warps per (sequence,
+// query head).  Warp 0 forms M (max of the splits' running maxima), L (sum of
+// L_s * 2^(M_s - M)) and the weights w_s = 2^(M_s - M) / L into shared
+// memory; then warp k sums w_s times the partials of splits s = k, k+4, ...
+// (all of its loads in flight at once) and the four sums are added.
+// Launched with programmatic serialization right after the attention kernel;
+// it waits for it before reading anything, and lets its own successor launch
+// first: the successor (the next layer's attention, a GEMV) reads only
+// constant data (its K/V cache, weights) before its own griddepcontrol.wait,
+// which returns only once this kernel, and so the attention, has completed.
+constexpr int kCombWarps = 4;
+constexpr int kCombUnroll = 8;
+
+template <int HD, int G>
+__global__ void __launch_bounds__(32 * kCombWarps)
+decode_combine_kernel(const DecodeArgs a, const DecodeSeq tab) {
+    constexpr int MLS = 2 * (G < 2 ? 2 : G);
+    constexpr int V4 = HD / 4;  // float4 per head: 32 or 16 lanes busy
+    __shared__ float s_w[kMaxSplitsPerSeq];
+    __shared__ float4 s_acc[kCombWarps][32];
+    grid_launch_dependents();
+    grid_dependency_wait();
+    const int seq = blockIdx.x, qh = blockIdx.y, kvh = qh / G, g = qh - kvh * G;
+    const int nsplit = tab.split0[seq + 1] - tab.split0[seq];
+    if (nsplit <= 1) return;  // the attention kernel wrote this output itself
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const size_t pfirst = size_t(kvh) * tab.split0[tab.n_seq] + tab.split0[seq];
+    const float *ml = a.part_ml + pfirst * MLS + 2 * g;
+    if (warp == 0) {
+        float M = -INFINITY;
+        for (int sp = lane; sp < nsplit; sp += 32) M = fmaxf(M, ml[size_t(sp) * MLS]);
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+        float L = 0.f;
+        for (int sp = lane; sp < nsplit; sp += 32)
+            L += ml[size_t(sp) * MLS + 1] * fast_exp2(ml[size_t(sp) * MLS] - M);
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+        const float inv = 1.f / L;
+        for (int sp = lane; sp < nsplit; sp += 32) s_w[sp] = fast_exp2(ml[size_t(sp) * MLS] - M) * inv;
+    }
+    // the partials do not depend on the weights: start loading them now
+    const float *po = a.part_o + pfirst * (G * HD) + g * HD + 4 * (lane < V4 ? lane : 0);
+    float4 v[kCombUnroll];
+    int sp0 = warp;
+#pragma unroll
+    for (int u = 0; u < kCombUnroll; ++u) {
+        const int sp = sp0 + u * kCombWarps;
+        v[u] = sp < nsplit ? *reinterpret_cast<const float4 *>(po + size_t(sp) * (G * HD))
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    __syncthreads();
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (;;) {
+#pragma unroll
+        for (int u = 0; u < kCombUnroll; ++u) {
+            const int sp = sp0 + u * kCombWarps;
+            if (sp < nsplit) {
+                const float w = s_w[sp];
+                acc.x = fmaf(w, v[u].x, acc.x);
+                acc.y = fmaf(w, v[u].y, acc.y);
+                acc.z = fmaf(w, v[u].z, acc.z);
+                acc.w = fmaf(w, v[u].w, acc.w);
+            }
+        }
+        sp0 += kCombUnroll * kCombWarps;
+        if (sp0 >= nsplit) break;
+#pragma unroll
+        for (int u = 0; u < kCombUnroll; ++u) {
+            const int sp = sp0 + u * kCombWarps;
+            v[u] = sp < nsplit ? *reinterpret_cast<const float4 *>(po + size_t(sp) * (G * HD))
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    }
+    s_acc[warp][lane] = acc;
+    __syncthreads();
+    if (warp == 0 && lane < V4) {
+        float4 r = s_acc[0][lane];
+#pragma unroll
+        for (int k = 1; k < kCombWarps; ++k) {
+            const float4 t = s_acc[k][lane];
+            r.x += t.x; r.y += t.y; r.z += t.z; r.w += t.w;
+        }
+        float *out = a.out + (size_t(seq) * a.n_kv * G + qh) * HD;
+        *reinterpret_cast<float4 *>(out + 4 * lane) = r;
+    }
+}
+
 template <int HD, int G, int NT>
 int launch_t(leap_ctx *c, const DecodeArgs &a, const DecodeSeq &tab, int total_splits,
-             bool overlap) {
+             bool overlap, bool tail) {
     using C = Cfg<HD, G, NT>;
     static bool attr_set[kMaxDevices] = {};  // the attribute is per device
     if (c->device >= kMaxDevices) return cuda_status(cudaErrorInvalidDevice, "device");
     if (!attr_set[c->device]) {
-        cudaError_t e = cudaFuncSetAttribute(decode_attn_kernel<HD, G, NT>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             int(C::kSmem));
-        if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(decode)");
+        for (auto fn : {decode_attn_kernel<HD, G, NT, true>, decode_attn_kernel<HD, G, NT, false>}) {
+            cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 int(C::kSmem));
+            if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(decode)");
+        }
         attr_set[c->device] = true;
     }
     cudaLaunchConfig_t cfg = {};
@@ -474,8 +567,23 @@ int launch_t(leap_ctx *c, const DecodeArgs &a, const DecodeSeq &tab, int total_s
     attr[0].val.programmaticStreamSerializationAllowed = overlap ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cuda_status(cudaLaunchKernelEx(&cfg, decode_attn_kernel<HD, G, NT>, a, tab),
-                       "decode_attn_kernel launch");
+    const bool combine = !tail && total_splits > tab.n_seq;  // some sequence has splits
+    const int st = cuda_status(
+        cudaLaunchKernelEx(&cfg, combine ? decode_attn_kernel<HD, G, NT, false>
+                                         : decode_attn_kernel<HD, G, NT, true>, a, tab),
+        "decode_attn_kernel launch");
+    if (st != LEAP_OK || !combine) return st;
+    cudaLaunchConfig_t cc = {};
+    cc.gridDim = dim3(tab.n_seq, c->n_kv * G);
+    cc.blockDim = dim3(32 * kCombWarps);
+    cc.stream = c->stream;
+    cudaLaunchAttribute cattr[1];
+    cattr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    cattr[0].val.programmaticStreamSerializationAllowed = 1;  // it waits before reading
+    cc.attrs = cattr;
+    cc.numAttrs = 1;
+    return cuda_status(cudaLaunchKernelEx(&cc, decode_combine_kernel<HD, G>, a, tab),
+                       "decode_combine_kernel launch");
 }
 
 }  // namespace
@@ -517,16 +625,17 @@ int max_decode_parts(int hd, int n_kv, int max_batch, int max_seq_pad, int num_s
 
 namespace {
 template <int NT>
-int launch_width(leap_ctx *c, const DecodeArgs &a, const DecodeSeq &tab, int total, bool overlap) {
+int launch_width(leap_ctx *c, const DecodeArgs &a, const DecodeSeq &tab, int total, bool overlap,
+                 bool tail) {
     switch (c->hd * 100 + c->group) {
-        case 12801: return launch_t<128, 1, NT>(c, a, tab, total, overlap);
-        case 12802: return launch_t<128, 2, NT>(c, a, tab, total, overlap);
-        case 12804: return launch_t<128, 4, NT>(c, a, tab, total, overlap);
-        case 12808: return launch_t<128, 8, NT>(c, a, tab, total, overlap);
-        case 6401: return launch_t<64, 1, NT>(c, a, tab, total, overlap);
-        case 6402: return launch_t<64, 2, NT>(c, a, tab, total, overlap);
-        case 6404: return launch_t<64, 4, NT>(c, a, tab, total, overlap);
-        case 6408: return launch_t<64, 8, NT>(c, a, tab, total, overlap);
+        case 12801: return launch_t<128, 1, NT>(c, a, tab, total, overlap, tail);
+        case 12802: return launch_t<128, 2, NT>(c, a, tab, total, overlap, tail);
+        case 12804: return launch_t<128, 4, NT>(c, a, tab, total, overlap, tail);
+        case 12808: return launch_t<128, 8, NT>(c, a, tab, total, overlap, tail);
+        case 6401: return launch_t<64, 1, NT>(c, a, tab, total, overlap, tail);
+        case 6402: return launch_t<64, 2, NT>(c, a, tab, total, overlap, tail);
+        case 6404: return launch_t<64, 4, NT>(c, a, tab, total, overlap, tail);
+        case 6408: return launch_t<64, 8, NT>(c, a, tab, total, overlap, tail);
         default:
             set_error("unsupported head_dim %d / kv_mul %d", c->hd, c->group);
             return LEAP_ERR_INVALID;
@@ -555,6 +664,8 @@ int launch_decode(leap_ctx *c, int layer, const DecodeSeq &seqs, const float *q,
     // Split-KV CTA shape: 128 threads, two CTAs per SM (measured fastest at
     // ctx 1k-8k); impl 3 selects 256 threads, one per SM (half the splits).
     const int nt = (c->decode_impl == 3) ? 256 : 128;
+    // impl 4: the splits are combined by a second launch; else by the last CTA
+    const bool tail = c->decode_impl != 4;
     DecodeSeq tab = seqs;
     plan_decode(c, tab, nt);
     const int total = tab.split0[tab.n_seq];
@@ -583,8 +694,8 @@ int launch_decode(leap_ctx *c, int layer, const DecodeSeq &seqs, const float *q,
     a.err = c->d_err;
     a.n_kv = c->n_kv;
     a.scale_log2 = kLog2e / sqrtf(float(c->hd));
-    const int st = nt == 128 ? launch_width<128>(c, a, tab, total, overlap)
-                             : launch_width<256>(c, a, tab, total, overlap);
+    const int st = nt == 128 ? launch_width<128>(c, a, tab, total, overlap, tail)
+                             : launch_width<256>(c, a, tab, total, overlap, tail);
     if (st == LEAP_OK) {
         c->parity ^= 1;
         c->last_written_layer = layer;

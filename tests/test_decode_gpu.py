@@ -34,7 +34,9 @@ def _run(ctx, layer, pos, q, kn, vn, kr, vr):
     return out.cpu().numpy(), kk[0], vv[0]
 
 
-IMPLS = [1, 2, 3]  # split-KV (the auto choice here), cluster kernel, wide split-KV
+# split-KV with last-CTA combine (the auto choice here), cluster kernel, wide
+# split-KV, split-KV with a separate combine launch
+IMPLS = [1, 2, 3, 4]
 
 
 @pytest.mark.parametrize("impl", IMPLS)
