@@ -504,6 +504,7 @@ def run_model(args):
     dev = torch.device("cuda", local)
     if world > 1:
         import datetime
+        os.environ.setdefault("TORCH_NCCL_SHOW_EAGER_INIT_P2P_SERIALIZATION_WARNING", "false")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
     cfg = ModelConfig(*shape)
     lb, le = stage_range(cfg.n_layers, rank, world)
@@ -511,7 +512,11 @@ def run_model(args):
     eng = Transformer.synthetic(cfg, q8, seed=SEED, device=local, rope_theta=theta,
                                 layer_range=(lb, le), max_chunk=chunk)
     eng.bind_torch_stream()
-    stage = PipelineStage(eng, cfg.dim, dev, max_chunk=chunk, rank=rank, world=world)
+    comm = None
+    if world > 1:
+        from leap_b200.pipeline import NativeComm, TorchComm
+        comm = NativeComm(rank, world, local) if args.comm == "native" else TorchComm()
+    stage = PipelineStage(eng, cfg.dim, dev, max_chunk=chunk, rank=rank, world=world, comm=comm)
     prompt = [int(t) for t in np.random.default_rng(SEED).integers(0, cfg.vocab_size,
                                                                      prompt_len)]
     stream = torch.cuda.current_stream(dev)
@@ -592,6 +597,9 @@ def run_model(args):
                                    f"then greedy decode", "model": args.model,
                        "global_batch": 1, "seq_len": prompt_len + warm + steps,
                        "parallelism": f"pp{world}" if world > 1 else "single",
+                       "stage_transport": (("leap_pp (NCCL p2p)" if args.comm == "native"
+                                            else "torch.distributed p2p") if world > 1
+                                           else None),
                        "stages": [list(stage_range(cfg.n_layers, r, world))
                                   for r in range(world)],
                        "l2": f"inputs > L2: {per_tok / 1e9:.2f} GB of weights and KV per token"},
@@ -609,6 +617,8 @@ def run_model(args):
         }
     eng.close()
     if world > 1:
+        torch.cuda.synchronize(dev)
+        comm.close()
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -691,6 +701,76 @@ def model_cpu_baseline(name, ctx, seconds):
             "kind": "reference", "sample": sample, "ms_per_token": round(sec * 1e3, 2)}
 
 
+def run_batched(args):
+    """ragged batched decode, 64 sequences with contexts
+    drawn uniform in [512, 8192] from seed 1 (numpy default_rng), Llama-3-8B
+    heads, fused RoPE + append.  One step = one batched launch per layer over
+    2 layers (each layer's caches hold 2.28 GB, far beyond L2).  Bytes per
+    launch = the sum over sequences of the config-2 formula."""
+    import torch
+    from leap_b200 import AttentionContext
+    dev = torch.device("cuda", 0)
+    n_seq, n_layers = 64, 2
+    ctxs = np.random.default_rng(1).integers(512, 8193, n_seq)
+    max_seq = int(ctxs.max())
+    ctx = AttentionContext(n_layers, N_HEADS, N_KV, HD, max_seq, max_batch=n_seq, theta=THETA)
+    ctx.set_decode_impl(args.decode_impl)
+    g = torch.Generator(device=dev)
+    g.manual_seed(1)
+    for layer in range(n_layers):
+        for i, c in enumerate(ctxs):
+            kr = torch.randn(int(c) - 1, N_KV, HD, device=dev, generator=g)
+            vr = torch.randn(int(c) - 1, N_KV, HD, device=dev, generator=g)
+            ctx.kv_write(i, layer, 0, kr, vr)
+    q = torch.randn(n_layers, n_seq, N_HEADS, HD, device=dev, generator=g)
+    kn = torch.randn(n_layers, n_seq, N_KV, HD, device=dev, generator=g)
+    vn = torch.randn(n_layers, n_seq, N_KV, HD, device=dev, generator=g)
+    out = torch.empty_like(q)
+    slots = np.arange(n_seq, dtype=np.int32)
+    pos = (ctxs - 1).astype(np.int32)
+    ctx.bind_torch_stream()
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        for layer in range(n_layers):
+            ctx.decode_batched(layer, slots, pos, q[layer], kn[layer], vn[layer], out[layer])
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize(dev)
+    sampler = ClockSampler(0)
+    sampler.start()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    clocks = sampler.stop()
+    ctx.sync()
+    ms = e0.elapsed_time(e1) / args.steps
+    per_launch = sum(algorithmic_bytes(N_HEADS, N_KV, HD, int(c)) for c in ctxs)
+    value = per_launch * n_layers / (ms / 1e3) / 1e9
+    peak, peak_kind = load_peaks()
+    line = {"metric": "batched decode-attn KV GB/s", "value": round(value, 2), "unit": "GB/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": max(args.warmup, 3),
+            "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "config3: 64 ragged sequences, ctx ~U[512,8192] seed 1, "
+                                   "Llama-3-8B heads, fused RoPE + append",
+                       "global_batch": n_seq, "seq_len": int(ctxs.max()),
+                       "total_ctx": int(ctxs.sum()),
+                       "l2": f"inputs > L2: {per_launch / 1e9:.2f} GB per launch"},
+            "roofline": {"bound": "hbm", "achieved": round(value, 2), "peak": peak,
+                         "peak_kind": peak_kind, "unit": "GB/s", "frac": round(value / peak, 4),
+                         "bytes_per_launch": int(per_launch),
+                         "mean_launch_us": round(ms / n_layers * 1e3, 2)},
+            "gpu_launches": n_layers * args.steps, "clocks": clocks}
+    ctx.close()
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -711,9 +791,13 @@ def main():
                     help="0 tcgen05 3xTF32, 1 CUDA-core FP32")
     ap.add_argument("--layers", type=int, default=N_LAYERS)
     ap.add_argument("--ctx", type=int, default=CTX)
+    ap.add_argument("--batched", action="store_true",
+                    help="benchmark config 3 (64 ragged sequences) instead")
     ap.add_argument("--model", choices=sorted(MODELS), default=None,
                     help="end-to-end decode of a whole model (pipeline over the ranks)")
     ap.add_argument("--prompt", type=int, default=0, help="prompt tokens for --model")
+    ap.add_argument("--comm", choices=["native", "torch"], default="native",
+                    help="stage transport for --model on N > 1 ranks")
     args = ap.parse_args()
     args.steps_given = args.steps is not None
     if args.steps is None:
@@ -727,6 +811,8 @@ def main():
             run_reference_arm(args)
     elif args.model:
         run_model(args)
+    elif args.batched:
+        run_batched(args)
     elif args.prefill:
         run_prefill(args)
     else:

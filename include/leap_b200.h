@@ -47,6 +47,7 @@ extern "C" {
 #define LEAP_ERR_CUDA 2      /* a CUDA runtime call failed                     */
 #define LEAP_ERR_DEVICE 3    /* a kernel reported an error (bounded wait hit)  */
 #define LEAP_ERR_NOMEM 4     /* device allocation failed                       */
+#define LEAP_ERR_COMM 5      /* a stage-to-stage transfer failed or timed out  */
 
 typedef struct leap_ctx leap_ctx; /* opaque */
 
@@ -375,6 +376,38 @@ LEAP_API int leap_op_set_q8_gemv(int impl);
 /* Greedy sampling (Sampler.cpp:20-120 at temperature 0): index of the
  * first maximum in the reference's scan order. */
 LEAP_API int leap_op_argmax(void *stream, int *token, const float *v, int n);
+
+/* ---- stage-to-stage transport (layer-range pipelines in one box) --------
+ * Replaces the reference's ring transport between a master and its workers
+ * (src/inference/FloatTransformer.cpp:772-793 and :800-946, TCP/UDP or the
+ * kernel module; src/inference/Transformer.h:17-23) for GPUs of one node:
+ * point-to-point NCCL sends over NVLink, ordered on the caller's stream.
+ * One process per GPU.  NCCL is loaded at run time (the process's own copy
+ * when it already has one).  Creation and every enqueue wait at most
+ * `timeout_ms` (0 = 60 s); on a timeout the communicator is aborted and the
+ * call returns LEAP_ERR_COMM. */
+typedef struct leap_pp leap_pp; /* opaque */
+
+/* Rank 0 creates the job's id (128 bytes) and hands it to every rank by any
+ * host channel (a TCP store, an MPI broadcast, a file). */
+LEAP_API int leap_pp_unique_id(void *id_out);
+LEAP_API int leap_pp_init(const void *id, int rank, int world, int device,
+                          int timeout_ms, leap_pp **out);
+/* x[bytes] of this stage to stage rank+1 / from stage rank-1 (device
+ * buffers; stream = cudaStream_t, NULL = default stream). */
+LEAP_API int leap_pp_send_next(leap_pp *pp, const void *buf, size_t bytes,
+                               void *stream);
+LEAP_API int leap_pp_recv_prev(leap_pp *pp, void *buf, size_t bytes,
+                               void *stream);
+/* Any peer (the last stage returns the sampled token id to stage 0). */
+LEAP_API int leap_pp_send(leap_pp *pp, int peer, const void *buf, size_t bytes,
+                          void *stream);
+LEAP_API int leap_pp_recv(leap_pp *pp, int peer, void *buf, size_t bytes,
+                          void *stream);
+/* End every transfer in flight (a peer died or stopped answering); the
+ * communicator cannot be used afterwards.  Then leap_pp_destroy. */
+LEAP_API int leap_pp_abort(leap_pp *pp);
+LEAP_API int leap_pp_destroy(leap_pp *pp);
 
 #ifdef __cplusplus
 }

@@ -23,6 +23,7 @@ LEAP_ERR_INVALID = 1
 LEAP_ERR_CUDA = 2
 LEAP_ERR_DEVICE = 3
 LEAP_ERR_NOMEM = 4
+LEAP_ERR_COMM = 5
 
 
 class CtxDesc(ctypes.Structure):
@@ -106,6 +107,14 @@ SIGNATURES: dict[str, tuple] = {
     "leap_op_qmatmul": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                 c_int, c_int, c_int, c_int, c_void_p]),
     "leap_op_argmax": (c_int, [c_void_p, c_void_p, c_void_p, c_int]),
+    "leap_pp_unique_id": (c_int, [c_void_p]),
+    "leap_pp_init": (c_int, [c_void_p, c_int, c_int, c_int, c_int, ctypes.POINTER(c_void_p)]),
+    "leap_pp_send_next": (c_int, [c_void_p, c_void_p, ctypes.c_size_t, c_void_p]),
+    "leap_pp_recv_prev": (c_int, [c_void_p, c_void_p, ctypes.c_size_t, c_void_p]),
+    "leap_pp_send": (c_int, [c_void_p, c_int, c_void_p, ctypes.c_size_t, c_void_p]),
+    "leap_pp_recv": (c_int, [c_void_p, c_int, c_void_p, ctypes.c_size_t, c_void_p]),
+    "leap_pp_abort": (c_int, [c_void_p]),
+    "leap_pp_destroy": (c_int, [c_void_p]),
     "leap_op_set_q8_gemv": (c_int, [c_int]),
 }
 

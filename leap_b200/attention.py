@@ -198,7 +198,8 @@ class AttentionContext:
         return out
 
     def set_decode_impl(self, impl: int) -> None:
-        """0 = auto, 1 = split-KV, 2 = cluster kernel, 3 = wide split-KV."""
+        """0 = auto, 1 = split-KV, 2 = cluster kernel, 3 = wide split-KV,
+        4 = split-KV with a separate combine launch."""
         check(lib().leap_set_decode_impl(self.handle, impl))
 
     def cluster_capacity(self) -> int:

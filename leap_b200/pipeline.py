@@ -20,19 +20,79 @@ runs as N stages, one per GPU:
   sent straight from device memory, and no stage waits on its host between
   decode steps.
 
-`Comm` is torch.distributed point-to-point on the default process group
-(NCCL between GPUs; gloo for the CPU tests of the schedule).  The engine is
-anything with the stage operations of `leap_b200.Transformer` (`embed`,
-`embed_device`, `layers`, `head` on tensors).
+The hop goes through a transport object with `send(tensor, dst)` and
+`recv(tensor, src)`: `NativeComm` is the library's own stage transport
+(`leap_pp_*`, NCCL point-to-point over NVLink, bounded by a timeout and
+abortable), `TorchComm` is torch.distributed point-to-point on the default
+process group (used by the CPU tests of the schedule, over gloo).  The
+engine is anything with the stage operations of `leap_b200.Transformer`
+(`embed`, `embed_device`, `layers`, `head` on tensors).
 """
 from __future__ import annotations
 
+import ctypes
 import dataclasses
 
 import torch
 import torch.distributed as dist
 
-__all__ = ["stage_range", "PipelineStage", "StageTimes"]
+__all__ = ["stage_range", "PipelineStage", "StageTimes", "TorchComm", "NativeComm"]
+
+
+class TorchComm:
+    """Point-to-point on torch.distributed's default group."""
+
+    def send(self, t: torch.Tensor, dst: int) -> None:
+        dist.send(t, dst=dst)
+
+    def recv(self, t: torch.Tensor, src: int) -> None:
+        dist.recv(t, src=src)
+
+    def close(self) -> None:
+        pass
+
+
+class NativeComm:
+    """The library's stage transport (leap_pp_*): NCCL point-to-point over
+    NVLink, enqueued on the current torch stream.  The 128-byte job id is
+    made by rank 0 and handed to the others over the default process group
+    (any host channel would do)."""
+
+    def __init__(self, rank: int, world: int, device: int, timeout_ms: int = 60000):
+        from ._native import check, lib
+        self._lib, self._check = lib(), check
+        uid = ctypes.create_string_buffer(128)
+        if rank == 0:
+            check(self._lib.leap_pp_unique_id(uid))
+        if world > 1:
+            t = torch.frombuffer(bytearray(uid.raw), dtype=torch.uint8).clone()
+            if dist.get_backend() == "nccl":
+                t = t.cuda(device)
+            dist.broadcast(t, src=0)
+            uid = ctypes.create_string_buffer(bytes(t.cpu().tolist()), 128)
+        self._h = ctypes.c_void_p()
+        check(self._lib.leap_pp_init(uid, rank, world, device, timeout_ms, ctypes.byref(self._h)))
+
+    def _stream(self):
+        return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+    def send(self, t: torch.Tensor, dst: int) -> None:
+        self._check(self._lib.leap_pp_send(self._h, dst, ctypes.c_void_p(t.data_ptr()),
+                                           t.numel() * t.element_size(), self._stream()))
+
+    def recv(self, t: torch.Tensor, src: int) -> None:
+        self._check(self._lib.leap_pp_recv(self._h, src, ctypes.c_void_p(t.data_ptr()),
+                                           t.numel() * t.element_size(), self._stream()))
+
+    def abort(self) -> None:
+        """End transfers whose peer has gone (the communicator is unusable after)."""
+        if self._h:
+            self._lib.leap_pp_abort(self._h)
+
+    def close(self) -> None:
+        if self._h:
+            h, self._h = self._h, None
+            self._check(self._lib.leap_pp_destroy(h))
 
 
 def stage_range(n_layers: int, rank: int, world: int) -> tuple[int, int]:
@@ -54,8 +114,10 @@ class PipelineStage:
     `engine` holds this stage's layer range; `dim` is the model width;
     `device` is where activations live (a CUDA device, or CPU for gloo)."""
 
-    def __init__(self, engine, dim: int, device, max_chunk: int = 512, rank=None, world=None):
+    def __init__(self, engine, dim: int, device, max_chunk: int = 512, rank=None, world=None,
+                 comm=None):
         self.e = engine
+        self.comm = comm if comm is not None else TorchComm()
         self.rank = dist.get_rank() if rank is None else rank
         self.world = dist.get_world_size() if world is None else world
         self.first = self.rank == 0
@@ -75,19 +137,19 @@ class PipelineStage:
             else:
                 self.e.embed(tokens, x)
         else:
-            dist.recv(x, src=self.rank - 1)
+            self.comm.recv(x, self.rank - 1)
         self.e.layers(pos0, x)
         if not self.last:
-            dist.send(x, dst=self.rank + 1)
+            self.comm.send(x, self.rank + 1)
         return x
 
     def _token_to_first(self) -> None:
         if self.world == 1:
             return
         if self.last:
-            dist.send(self.tok, dst=0)
+            self.comm.send(self.tok, 0)
         elif self.first:
-            dist.recv(self.tok, src=self.world - 1)
+            self.comm.recv(self.tok, self.world - 1)
 
     # -- the reference's generate loop, split across stages ---------------------
     def prefill(self, prompt, pos0: int = 0, chunk: int | None = None) -> None:

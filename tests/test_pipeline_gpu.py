@@ -1,6 +1,7 @@
 """GPU (2 devices): the layer-range pipeline over NCCL gives the tokens of
 the single-GPU engine, bit for bit (the same kernels run on the same layers;
-only the hand-off of x[dim] between stages is new).
+only the hand-off of x[dim] between stages is new) — through the library's
+own stage transport (leap_pp_*) and through torch.distributed.
 
 Skipped unless two CUDA devices are visible.  Each stage is its own process
 (one per GPU) with a short process-group timeout.
@@ -21,11 +22,11 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _stage(rank, world, port, quantized, q):
+def _stage(rank, world, port, quantized, q, comm_kind):
     import torch.distributed as dist
 
     from leap_b200 import ModelConfig, Transformer
-    from leap_b200.pipeline import PipelineStage, stage_range
+    from leap_b200.pipeline import NativeComm, PipelineStage, TorchComm, stage_range
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
@@ -39,9 +40,11 @@ def _stage(rank, world, port, quantized, q):
         with Transformer.synthetic(cfg, quantized, seed=11, device=rank, layer_range=(lb, le),
                                    max_chunk=16) as eng:
             eng.bind_torch_stream()
-            st = PipelineStage(eng, cfg.dim, dev, max_chunk=16)
+            comm = NativeComm(rank, world, rank, 30000) if comm_kind == "native" else TorchComm()
+            st = PipelineStage(eng, cfg.dim, dev, max_chunk=16, comm=comm)
             toks = st.generate(prompt, 40, chunk=16)
             torch.cuda.synchronize()
+            comm.close()
         want = None
         if rank == 0:
             with Transformer.synthetic(cfg, quantized, seed=11, device=rank, max_chunk=16) as full:
@@ -55,15 +58,16 @@ def _stage(rank, world, port, quantized, q):
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("comm_kind", ["native", "torch"])
 @pytest.mark.parametrize("quantized", [False, True])
-def test_two_stage_pipeline_matches_single_gpu(cuda, quantized):
+def test_two_stage_pipeline_matches_single_gpu(cuda, quantized, comm_kind):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_stage, args=(r, 2, port, quantized, q)) for r in range(2)]
+    procs = [ctx.Process(target=_stage, args=(r, 2, port, quantized, q, comm_kind)) for r in range(2)]
     for p in procs:
         p.start()
     res = {}
