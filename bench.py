@@ -782,7 +782,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--eager", action="store_true", help="launch from Python, no CUDA graph")
     ap.add_argument("--decode-impl", type=int, default=0,
-                    help="0 auto, 1 split-KV kernel, 2 cluster kernel")
+                    help="0 auto, 1 split-KV + last-CTA combine, 2 cluster kernel, "
+                         "3 wide split-KV, 4 split-KV + combine launch")
     ap.add_argument("--no-overlap", action="store_true",
                     help="no programmatic dependent launch between layers")
     ap.add_argument("--prefill", type=int, default=0,

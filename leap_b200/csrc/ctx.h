@@ -104,7 +104,7 @@ int launch_decode(leap_ctx *c, int layer, const DecodeSeq &tab, const float *q,
                   const float *k_new, const float *v_new, float *out);
 
 // Fill tab.chunk / tab.split0 for the given positions; returns total splits.
-int plan_decode(const leap_ctx *c, DecodeSeq &tab, int nt);
+int plan_decode(const leap_ctx *c, DecodeSeq &tab, int shape);
 
 // decode_cluster.cu: co-resident 16-CTA clusters, and the launch.
 int decode_cluster_capacity(leap_ctx *c, int *n);

@@ -28,17 +28,18 @@
 namespace leap {
 namespace {
 
-// Two CTA shapes: NT = 128 threads, 16 KB tiles, two CTAs per SM; or
-// NT = 256 threads, 32 KB tiles, one CTA per SM (half as many splits, so a
-// shorter combine).  Three stages of K+V tiles either way.
+// CTA shapes (SH), three stages of K+V tiles each:
+//   0: 128 threads, 16 KB tiles, two CTAs per SM;
+//   1: 256 threads, 32 KB tiles, one CTA per SM (half as many splits).
 constexpr int kStages = 3;
 constexpr int kMaxSplitsPerSeq = 256;
 
-template <int HD, int G, int NT>
+template <int HD, int G, int SH>
 struct Cfg {
-    static constexpr int THREADS = NT;
-    static constexpr int WARPS = NT / 32;
-    static constexpr int TILE_BYTES = NT * 128;       // per tensor per stage
+    static constexpr int THREADS = SH == 0 ? 128 : 256;
+    static constexpr int MINB = SH == 1 ? 1 : 2;     // resident CTAs per SM
+    static constexpr int WARPS = THREADS / 32;
+    static constexpr int TILE_BYTES = SH == 1 ? 32768 : 16384;  // per tensor per stage
     static constexpr int kLpr0 = G * HD / 64;
     static constexpr int LPR = kLpr0 < 8 ? 8 : (kLpr0 > 32 ? 32 : kLpr0);
     static constexpr int RPW = 32 / LPR;             // rows per warp pass
@@ -80,10 +81,10 @@ struct DecodeArgs {
 // TAIL: the last CTA of a (sequence, kv head) combines its splits (ticket);
 // otherwise every CTA only publishes its partial and decode_combine_kernel,
 // launched right after, combines them.
-template <int HD, int G, int NT, bool TAIL>
-__global__ void __launch_bounds__(NT, 256 / NT)
+template <int HD, int G, int SH, bool TAIL>
+__global__ void __launch_bounds__(Cfg<HD, G, SH>::THREADS, Cfg<HD, G, SH>::MINB)
 decode_attn_kernel(const DecodeArgs a, const DecodeSeq tab) {
-    using C = Cfg<HD, G, NT>;
+    using C = Cfg<HD, G, SH>;
     extern __shared__ __align__(128) unsigned char smem_raw[];
     float *sK = reinterpret_cast<float *>(smem_raw);      // [kStages][TILE][HD]
     float *sV = sK + kStages * C::TILE * HD;
@@ -543,14 +544,14 @@ decode_combine_kernel(const DecodeArgs a, const DecodeSeq tab) {
     }
 }
 
-template <int HD, int G, int NT>
+template <int HD, int G, int SH>
 int launch_t(leap_ctx *c, const DecodeArgs &a, const DecodeSeq &tab, int total_splits,
              bool overlap, bool tail) {
-    using C = Cfg<HD, G, NT>;
+    using C = Cfg<HD, G, SH>;
     static bool attr_set[kMaxDevices] = {};  // the attribute is per device
     if (c->device >= kMaxDevices) return cuda_status(cudaErrorInvalidDevice, "device");
     if (!attr_set[c->device]) {
-        for (auto fn : {decode_attn_kernel<HD, G, NT, true>, decode_attn_kernel<HD, G, NT, false>}) {
+        for (auto fn : {decode_attn_kernel<HD, G, SH, true>, decode_attn_kernel<HD, G, SH, false>}) {
             cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  int(C::kSmem));
             if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(decode)");
@@ -559,7 +560,7 @@ int launch_t(leap_ctx *c, const DecodeArgs &a, const DecodeSeq &tab, int total_s
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(total_splits, c->n_kv);
-    cfg.blockDim = dim3(NT);
+    cfg.blockDim = dim3(C::THREADS);
     cfg.dynamicSmemBytes = C::kSmem;
     cfg.stream = c->stream;
     cudaLaunchAttribute attr[1];
@@ -569,8 +570,8 @@ int launch_t(leap_ctx *c, const DecodeArgs &a, const DecodeSeq &tab, int total_s
     cfg.numAttrs = 1;
     const bool combine = !tail && total_splits > tab.n_seq;  // some sequence has splits
     const int st = cuda_status(
-        cudaLaunchKernelEx(&cfg, combine ? decode_attn_kernel<HD, G, NT, false>
-                                         : decode_attn_kernel<HD, G, NT, true>, a, tab),
+        cudaLaunchKernelEx(&cfg, combine ? decode_attn_kernel<HD, G, SH, false>
+                                         : decode_attn_kernel<HD, G, SH, true>, a, tab),
         "decode_attn_kernel launch");
     if (st != LEAP_OK || !combine) return st;
     cudaLaunchConfig_t cc = {};
@@ -588,9 +589,11 @@ int launch_t(leap_ctx *c, const DecodeArgs &a, const DecodeSeq &tab, int total_s
 
 }  // namespace
 
-int plan_decode(const leap_ctx *c, DecodeSeq &tab, int nt) {
-    const int tile = nt * 128 / (c->hd * 4);
-    const long cap_rows = 2048L * nt / (c->hd * 4 * 2);  // 256/512 KB of K+V per CTA
+int plan_decode(const leap_ctx *c, DecodeSeq &tab, int shape) {
+    const int tile_bytes = shape == 1 ? 32768 : 16384;
+    const int per_sm = shape == 1 ? 1 : 2;
+    const int tile = tile_bytes / (c->hd * 4);
+    const long cap_rows = 16L * tile_bytes / (c->hd * 4 * 2);  // 256/512 KB of K+V per CTA
     long total = 0;
     int max_ctx = 0;
     for (int i = 0; i < tab.n_seq; ++i) {
@@ -599,7 +602,7 @@ int plan_decode(const leap_ctx *c, DecodeSeq &tab, int nt) {
         if (ctx > max_ctx) max_ctx = ctx;
     }
     const long rows = total * c->n_kv;
-    const long target = long(256 / nt) * c->num_sms;  // one wave
+    const long target = long(per_sm) * c->num_sms;  // one wave
     long chunk = (rows + target - 1) / target;
     if (chunk > cap_rows) chunk = cap_rows;
     const long min_chunk = (max_ctx + kMaxSplitsPerSeq - 1) / kMaxSplitsPerSeq;
@@ -624,18 +627,18 @@ int max_decode_parts(int hd, int n_kv, int max_batch, int max_seq_pad, int num_s
 }
 
 namespace {
-template <int NT>
+template <int SH>
 int launch_width(leap_ctx *c, const DecodeArgs &a, const DecodeSeq &tab, int total, bool overlap,
                  bool tail) {
     switch (c->hd * 100 + c->group) {
-        case 12801: return launch_t<128, 1, NT>(c, a, tab, total, overlap, tail);
-        case 12802: return launch_t<128, 2, NT>(c, a, tab, total, overlap, tail);
-        case 12804: return launch_t<128, 4, NT>(c, a, tab, total, overlap, tail);
-        case 12808: return launch_t<128, 8, NT>(c, a, tab, total, overlap, tail);
-        case 6401: return launch_t<64, 1, NT>(c, a, tab, total, overlap, tail);
-        case 6402: return launch_t<64, 2, NT>(c, a, tab, total, overlap, tail);
-        case 6404: return launch_t<64, 4, NT>(c, a, tab, total, overlap, tail);
-        case 6408: return launch_t<64, 8, NT>(c, a, tab, total, overlap, tail);
+        case 12801: return launch_t<128, 1, SH>(c, a, tab, total, overlap, tail);
+        case 12802: return launch_t<128, 2, SH>(c, a, tab, total, overlap, tail);
+        case 12804: return launch_t<128, 4, SH>(c, a, tab, total, overlap, tail);
+        case 12808: return launch_t<128, 8, SH>(c, a, tab, total, overlap, tail);
+        case 6401: return launch_t<64, 1, SH>(c, a, tab, total, overlap, tail);
+        case 6402: return launch_t<64, 2, SH>(c, a, tab, total, overlap, tail);
+        case 6404: return launch_t<64, 4, SH>(c, a, tab, total, overlap, tail);
+        case 6408: return launch_t<64, 8, SH>(c, a, tab, total, overlap, tail);
         default:
             set_error("unsupported head_dim %d / kv_mul %d", c->hd, c->group);
             return LEAP_ERR_INVALID;
@@ -663,11 +666,11 @@ int launch_decode(leap_ctx *c, int layer, const DecodeSeq &seqs, const float *q,
     }
     // Split-KV CTA shape: 128 threads, two CTAs per SM (measured fastest at
     // ctx 1k-8k); impl 3 selects 256 threads, one per SM (half the splits).
-    const int nt = (c->decode_impl == 3) ? 256 : 128;
+    const int shape = c->decode_impl == 3 ? 1 : 0;
     // impl 4: the splits are combined by a second launch; else by the last CTA
     const bool tail = c->decode_impl != 4;
     DecodeSeq tab = seqs;
-    plan_decode(c, tab, nt);
+    plan_decode(c, tab, shape);
     const int total = tab.split0[tab.n_seq];
     if (long(total) * c->n_kv > c->max_parts) {
         set_error("decode plan needs %d partials, scratch holds %d", total * c->n_kv,
@@ -694,8 +697,8 @@ int launch_decode(leap_ctx *c, int layer, const DecodeSeq &seqs, const float *q,
     a.err = c->d_err;
     a.n_kv = c->n_kv;
     a.scale_log2 = kLog2e / sqrtf(float(c->hd));
-    const int st = nt == 128 ? launch_width<128>(c, a, tab, total, overlap, tail)
-                             : launch_width<256>(c, a, tab, total, overlap, tail);
+    const int st = shape == 0 ? launch_width<0>(c, a, tab, total, overlap, tail)
+                              : launch_width<1>(c, a, tab, total, overlap, tail);
     if (st == LEAP_OK) {
         c->parity ^= 1;
         c->last_written_layer = layer;

@@ -124,7 +124,7 @@ extern "C" int leap_attn_decode_noalloc(void *stream, int n_heads, int n_kv_head
     tab.pos[0] = pos;
     tab.slot[0] = 0;
     DecodeSeq planned = tab;
-    const int total = plan_decode(&shim, planned, 128);
+    const int total = plan_decode(&shim, planned, 0);  // the 128-thread shape
     if (long(total) * n_kv_heads > shim.max_parts) {
         set_error("noalloc decode: context %d needs %d split-KV partials, the %zu-byte scratch "
                   "holds %d",
