@@ -32,6 +32,7 @@ constexpr int kTcHd = 128;       // head_dim handled here
 constexpr int kTcThreads = 128;
 constexpr uint32_t kColQhi = 0, kColQlo = 128, kColS = 256, kColPlo = 320, kColO = 384;
 constexpr uint32_t kTmemCols = 512;
+constexpr float kTcMaxLag = 8.0f;  // log2 of how far the running max may trail
 
 // shared-memory layout (bytes from a 1024-byte aligned base)
 constexpr uint32_t kOffKhi = 0;                    // 4 chunks x 64 rows x 128 B
@@ -233,20 +234,26 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const TcArgs 
                 s[h][c] = (key <= qp && key < kv_end) ? s[h][c] * a.scale_log2 : -INFINITY;
                 mt = fmaxf(mt, s[h][c]);
             }
-        const float alpha = (m == -INFINITY) ? 0.f : fast_exp2(m - mt);
+        // The running max moves (and O in TMEM is rescaled: 4 loads, 128
+        // multiplies and 4 stores per thread) only when the tile's max
+        // exceeds it by more than 2^8; otherwise the probabilities of this
+        // tile are formed against the old max and are at most 256, which
+        // FP32 carries without loss.  The result O / l is the same function.
+        const bool move = (m == -INFINITY) || (mt > m + kTcMaxLag);
+        const float alpha = move ? ((m == -INFINITY) ? 0.f : fast_exp2(m - mt)) : 1.f;
+        if (move) m = mt;
         float rs = 0.f;
         float phi[2][32], plo[2][32];
 #pragma unroll
         for (int h = 0; h < 2; ++h)
 #pragma unroll
             for (int c = 0; c < 32; ++c) {
-                const float p = (s[h][c] == -INFINITY) ? 0.f : fast_exp2(s[h][c] - mt);
+                const float p = (s[h][c] == -INFINITY) ? 0.f : fast_exp2(s[h][c] - m);
                 rs += p;
                 phi[h][c] = tc::tf32_hi(p);
                 plo[h][c] = p - phi[h][c];
             }
         l = l * alpha + rs;
-        m = mt;
         tc::st32(tmem + lane_off + kColS, phi[0]);
         tc::st32(tmem + lane_off + kColS + 32, phi[1]);
         tc::st32(tmem + lane_off + kColPlo, plo[0]);
