@@ -49,6 +49,25 @@ THETA = 500000.0
 SEED = 0
 
 
+# The one JSON result line goes to the process's original stdout; everything
+# else written to file descriptor 1 (NCCL's version banner, native libraries)
+# is sent to stderr, so stdout carries exactly that line.
+_RESULT_OUT = None
+
+
+def emit(obj) -> None:
+    out = _RESULT_OUT if _RESULT_OUT is not None else sys.stdout
+    out.write(json.dumps(obj) + "\n")
+    out.flush()
+
+
+def _keep_stdout_for_result() -> None:
+    global _RESULT_OUT
+    sys.stdout.flush()
+    _RESULT_OUT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
+
+
 def algorithmic_bytes(n_heads, n_kv, hd, ctx):
     """Bytes one decode launch must move: K and V rows read (ctx rows), q in,
     new k/v in, new k/v appended, out written."""
@@ -220,7 +239,7 @@ def run_reference_arm(args):
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 def workload_config(n, n_layers=N_LAYERS, ctx=CTX):
@@ -403,7 +422,7 @@ def run_gpu_arm(args):
                       "(4 distinct 67 MB layer caches cycled)",
             "ms_per_step": round(sec * 1e3, 2)}
     if rank == 0:
-        print(json.dumps(line), flush=True)
+        emit(line)
 
 
 def run_prefill(args):
@@ -446,17 +465,17 @@ def run_prefill(args):
     line = {"metric": "causal prefill TFLOP/s (logical FP32)", "value": round(tflops, 2),
             "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(ms, 4), "higher_is_better": True, "dtype": "f32 (3xTF32)"
-            if args.prefill_impl == 0 else "f32",
+            if args.prefill_impl != 1 else "f32",
             "config": {"workload": f"config4: causal prefill L={L}, Llama-3-8B heads, batch 1",
-                       "seq_len": L, "impl": "tcgen05 3xTF32" if args.prefill_impl == 0
-                       else "CUDA-core FP32"},
+                       "seq_len": L, "impl": {0: "tcgen05 3xTF32", 1: "CUDA-core FP32",
+                                2: "tcgen05 3xTF32 pipelined"}[args.prefill_impl]},
             "roofline": {"bound": "tensor", "achieved": round(tflops, 2),
                          "tensor_tflops_issued": round(3 * tflops, 2)
-                         if args.prefill_impl == 0 else None,
+                         if args.prefill_impl != 1 else None,
                          "peak": peak, "peak_kind": "measured bf16 dense (TF32 is half)",
                          "unit": "TFLOP/s", "frac": round(tflops / peak, 4)}}
     ctx.close()
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 # ---------------------------------------------------------------------------
@@ -625,7 +644,7 @@ def run_model(args):
         line["cpu_baseline"] = model_cpu_baseline(args.model, prompt_len + warm + steps // 2,
                                                   args.cpu_seconds)
     if rank == 0:
-        print(json.dumps(line), flush=True)
+        emit(line)
 
 
 def run_model_reference(args):
@@ -637,7 +656,7 @@ def run_model_reference(args):
     prompt_len = args.prompt or prompt_len
     cb = model_cpu_baseline(args.model, prompt_len + gen // 2, max(args.cpu_seconds, 5.0))
     if cb is None:
-        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref was not built"}))
+        emit({"impl": "reference", "unavailable": "oracle/_ref was not built"})
         return
     line = {"impl": "reference", "metric": f"decode tok/s ({args.model})",
             "value": cb["value"], "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
@@ -649,7 +668,7 @@ def run_model_reference(args):
             "cpu_baseline": cb,
             "e2e": {"value": cb["value"], "unit": "tok/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 def model_cpu_baseline(name, ctx, seconds):
@@ -768,7 +787,7 @@ def run_batched(args):
                          "mean_launch_us": round(ms / n_layers * 1e3, 2)},
             "gpu_launches": n_layers * args.steps, "clocks": clocks}
     ctx.close()
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 def main():
@@ -789,7 +808,7 @@ def main():
     ap.add_argument("--prefill", type=int, default=0,
                     help="benchmark config 4 (causal prefill of this many tokens) instead")
     ap.add_argument("--prefill-impl", type=int, default=0,
-                    help="0 tcgen05 3xTF32, 1 CUDA-core FP32")
+                    help="0 tcgen05 3xTF32, 1 CUDA-core FP32, 2 tcgen05 3xTF32 pipelined")
     ap.add_argument("--layers", type=int, default=N_LAYERS)
     ap.add_argument("--ctx", type=int, default=CTX)
     ap.add_argument("--batched", action="store_true",
@@ -800,6 +819,7 @@ def main():
     ap.add_argument("--comm", choices=["native", "torch"], default="native",
                     help="stage transport for --model on N > 1 ranks")
     args = ap.parse_args()
+    _keep_stdout_for_result()
     args.steps_given = args.steps is not None
     if args.steps is None:
         args.steps = 20

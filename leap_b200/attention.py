@@ -213,5 +213,6 @@ class AttentionContext:
         check(lib().leap_set_overlap(self.handle, int(bool(enable))))
 
     def set_prefill_impl(self, impl: int) -> None:
-        """0 = tensor-core 3xTF32 kernel, 1 = CUDA-core FP32 kernel."""
+        """0 = tensor-core 3xTF32 kernel, 1 = CUDA-core FP32 kernel,
+        2 = tensor-core 3xTF32 kernel pipelined across warp roles."""
         check(lib().leap_set_prefill_impl(self.handle, impl))

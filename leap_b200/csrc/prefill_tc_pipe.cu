@@ -1,0 +1,426 @@
+// prefill_tc_pipe.cu — causal prefill attention on tcgen05 tensor cores,
+// 3xTF32, software-pipelined across three roles.
+//
+// Semantics as prefill_tc.cu (the reference block run for pos0..pos0+n-1 in
+// order, src/inference/FloatTransformer.cpp:404-662 and main.cpp:80-89):
+// the append kernel has rotated q into `qrot` and written the chunk's rotated
+// k and raw v into the cache.  This kernel overlaps the three kinds of work
+// that prefill_tc.cu runs one after another for every key tile:
+//
+//   warps 0-3  (128 threads, TMEM lanes = the CTA's 128 query rows): online
+//              softmax of S(j) in FP32 registers, P(j) hi/lo back to TMEM;
+//   warps 4-7  (128 threads): convert the FP32 K/V tile j+2 staged by bulk
+//              copies into TF32 hi/lo operand tiles (K-major, 128-byte
+//              swizzle; V transposed);
+//   warp 8     (lane 0): issue the bulk copies and every tcgen05.mma:
+//              S(j+1) = Q K(j+1)^T is computed while the softmax works on
+//              S(j), then O += P(j) V(j).
+//
+// Key tiles are 32 keys so that everything can be double-buffered:
+//   TMEM (512 columns): Q hi [0,128) Q lo [128,256) O [256,384)
+//                       S/P hi buffer b at 384+64b, P lo at 384+64b+32;
+//   shared memory: per buffer b, K hi/lo [32][128] and V^T hi/lo [128][32]
+//                  (4 x 16 KB) and FP32 staging K, V [32][128] (2 x 16 KB).
+// Products are hi*hi + hi*lo + lo*hi (3xTF32, ~2^-21 relative).  The running
+// max moves only when a row's max grows by more than 2^8 (see prefill_tc.cu).
+// All hand-offs are mbarriers; every wait is bounded and a timeout sets the
+// error word after draining what is in flight.
+#include "common.cuh"
+#include "ctx.h"
+#include "tc.cuh"
+
+namespace leap {
+namespace {
+
+constexpr int kPRows = 128;                  // query rows per CTA = TMEM lanes
+constexpr int kPKeys = 32;                   // keys per tile
+constexpr int kPHd = 128;
+constexpr int kPThreads = 288;               // 4 softmax + 4 convert + 1 issue warps
+constexpr uint32_t kPColQhi = 0, kPColQlo = 128, kPColO = 256, kPColS = 384;
+constexpr uint32_t kPTmemCols = 512;
+constexpr float kPMaxLag = 8.0f;
+
+// shared memory (bytes from a 1024-aligned base), buffer b = 0/1
+constexpr uint32_t kPOpBytes = kPKeys * kPHd * 4;             // 16 KB: one operand tile
+__host__ __device__ constexpr uint32_t kPOffKhi(int b) { return uint32_t(b) * 4 * kPOpBytes; }
+__host__ __device__ constexpr uint32_t kPOffKlo(int b) { return kPOffKhi(b) + kPOpBytes; }
+__host__ __device__ constexpr uint32_t kPOffVThi(int b) { return kPOffKhi(b) + 2 * kPOpBytes; }
+__host__ __device__ constexpr uint32_t kPOffVTlo(int b) { return kPOffKhi(b) + 3 * kPOpBytes; }
+__host__ __device__ constexpr uint32_t kPOffStK(int b) { return 8 * kPOpBytes + uint32_t(b) * 2 * kPOpBytes; }
+__host__ __device__ constexpr uint32_t kPOffStV(int b) { return kPOffStK(b) + kPOpBytes; }
+constexpr uint32_t kPSmemUsed = 12 * kPOpBytes;               // 192 KB
+constexpr size_t kPSmem = kPSmemUsed + 1024;
+
+struct PArgs {
+    const float *qrot;   // [n_tok][n_heads][128], rotated
+    const float *kc;     // kv head 0 of (slot, layer); heads head_stride apart
+    const float *vc;
+    size_t head_stride;
+    float *out;          // [n_tok][n_heads][128]
+    int *err;
+    int pos0, n_tok, n_heads;
+    float scale_log2;
+};
+
+struct PBars {
+    uint64_t q_ready;        // Q hi/lo in TMEM (4 softmax warps)
+    uint64_t st_full[2];     // staging b holds tile j (bulk-copy bytes)
+    uint64_t st_empty[2];    // converters done with staging b (4 warps)
+    uint64_t op_full[2];     // operand tiles b hold tile j (4 warps)
+    uint64_t op_empty[2];    // PV(j) done: operands b and S/P buffer b free (commit)
+    uint64_t s_full[2];      // S(j) done (commit)
+    uint64_t p_full[2];      // P(j) in TMEM, O rescaled if needed (4 warps)
+};
+
+__device__ __forceinline__ uint32_t par(int j) { return uint32_t(j >> 1) & 1u; }
+
+template <int G>
+__global__ void __launch_bounds__(kPThreads, 1) prefill_tc_pipe_kernel(const PArgs a) {
+    constexpr int BT = kPRows / G;  // tokens per CTA
+    extern __shared__ unsigned char smem_raw[];
+    __shared__ PBars bars;
+    __shared__ uint32_t tmem_base_sh;
+    __shared__ int s_fail;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    unsigned char *base = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+    const uint32_t sbase = smem_addr(base);
+
+    const int kvh = blockIdx.y;
+    const int t0 = (gridDim.x - 1 - blockIdx.x) * BT;  // longest rows first
+    const int t_last = min(t0 + BT, a.n_tok) - 1;
+    const int kv_end = a.pos0 + t_last + 1;
+    const int n_kt = (kv_end + kPKeys - 1) / kPKeys;
+    const float *gK = a.kc + size_t(kvh) * a.head_stride;
+    const float *gV = a.vc + size_t(kvh) * a.head_stride;
+
+    if (tid == 0) {
+        mbar_init(&bars.q_ready, 4);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&bars.st_full[b], 1);
+            mbar_init(&bars.st_empty[b], 4);
+            mbar_init(&bars.op_full[b], 4);
+            mbar_init(&bars.op_empty[b], 1);
+            mbar_init(&bars.s_full[b], 1);
+            mbar_init(&bars.p_full[b], 4);
+        }
+        s_fail = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0) {
+        tc::alloc(&tmem_base_sh, kPTmemCols);
+        tc::relinquish();
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = tmem_base_sh;
+
+    if (warp < 4) {
+        // ================= softmax warps: row `tid` of the CTA =================
+        const uint32_t lane_off = uint32_t(warp * 32) << 16;
+        const int my_tok = t0 + tid / G;
+        const int my_head = kvh * G + tid % G;
+        const int qp = a.pos0 + my_tok;
+        const bool row_valid = my_tok < a.n_tok;
+        {
+            const float *qrow = a.qrot + (size_t(my_tok) * a.n_heads + my_head) * kPHd;
+#pragma unroll 1
+            for (int c = 0; c < kPHd / 32; ++c) {
+                float hi[32], lo[32];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (row_valid) v = *reinterpret_cast<const float4 *>(qrow + c * 32 + 4 * i);
+                    const float x[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        hi[4 * i + e] = tc::tf32_hi(x[e]);
+                        lo[4 * i + e] = x[e] - hi[4 * i + e];
+                    }
+                }
+                tc::st32(tmem + lane_off + kPColQhi + 32 * c, hi);
+                tc::st32(tmem + lane_off + kPColQlo + 32 * c, lo);
+            }
+            tc::wait_st();
+            tc::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars.q_ready);
+        }
+        float m = -INFINITY, l = 0.f;
+        bool ok = true;
+        for (int j = 0; j < n_kt && ok; ++j) {
+            const int b = j & 1;
+            const int k0 = j * kPKeys;
+            ok = __all_sync(0xffffffffu, mbar_wait(&bars.s_full[b], par(j)));
+            if (!ok) break;
+            tc::fence_after_sync();
+            const uint32_t scol = kPColS + 64u * b;
+            float s[32];
+            tc::ld32(tmem + lane_off + scol, s);
+            tc::wait_ld();
+            float mt = m;
+#pragma unroll
+            for (int c = 0; c < 32; ++c) {
+                const int key = k0 + c;
+                s[c] = (key <= qp && key < kv_end) ? s[c] * a.scale_log2 : -INFINITY;
+                mt = fmaxf(mt, s[c]);
+            }
+            const bool move = (m == -INFINITY) || (mt > m + kPMaxLag);
+            const float alpha = move ? ((m == -INFINITY) ? 0.f : fast_exp2(m - mt)) : 1.f;
+            if (move) m = mt;
+            float rs = 0.f;
+            float phi[32], plo[32];
+#pragma unroll
+            for (int c = 0; c < 32; ++c) {
+                const float p = (s[c] == -INFINITY) ? 0.f : fast_exp2(s[c] - m);
+                rs += p;
+                phi[c] = tc::tf32_hi(p);
+                plo[c] = p - phi[c];
+            }
+            l = l * alpha + rs;
+            tc::st32(tmem + lane_off + scol, phi);
+            tc::st32(tmem + lane_off + scol + 32, plo);
+            // O holds PV(0..j-1): rescale rows whose max moved, once PV(j-1)
+            // has landed (PV(j) is issued only after this warp's arrival below)
+            if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+                ok = __all_sync(0xffffffffu, mbar_wait(&bars.op_empty[b ^ 1], par(j - 1)));
+                if (!ok) break;
+                tc::fence_after_sync();
+#pragma unroll 1
+                for (int c = 0; c < kPHd / 32; ++c) {
+                    float o[32];
+                    tc::ld32(tmem + lane_off + kPColO + 32 * c, o);
+                    tc::wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) o[i] *= alpha;
+                    tc::st32(tmem + lane_off + kPColO + 32 * c, o);
+                }
+            }
+            tc::wait_st();
+            tc::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars.p_full[b]);
+        }
+        if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&bars.op_empty[(n_kt - 1) & 1], par(n_kt - 1)));
+        if (ok) {
+            tc::fence_after_sync();
+            const float inv = 1.f / l;
+            float *dst = a.out + (size_t(my_tok) * a.n_heads + my_head) * kPHd;
+#pragma unroll 1
+            for (int c = 0; c < kPHd / 32; ++c) {
+                float o[32];
+                tc::ld32(tmem + lane_off + kPColO + 32 * c, o);
+                tc::wait_ld();
+                if (row_valid) {
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        float4 v;
+                        v.x = o[4 * i + 0] * inv;
+                        v.y = o[4 * i + 1] * inv;
+                        v.z = o[4 * i + 2] * inv;
+                        v.w = o[4 * i + 3] * inv;
+                        *reinterpret_cast<float4 *>(dst + 32 * c + 4 * i) = v;
+                    }
+                }
+            }
+        } else if (lane == 0) {
+            atomicExch(&s_fail, 1);
+        }
+    } else if (warp < 8) {
+        // ================= converter warps: staging -> TF32 hi/lo operands ======
+        const int ct = tid - 128;  // 0..127
+        bool ok = true;
+        for (int j = 0; j < n_kt && ok; ++j) {
+            const int b = j & 1;
+            const int nr = min(kPKeys, kv_end - j * kPKeys);
+            ok = mbar_wait(&bars.st_full[b], par(j));
+            if (ok && j >= 2) ok = mbar_wait(&bars.op_empty[b], par(j - 2));
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) break;
+            const float *stK = reinterpret_cast<const float *>(base + kPOffStK(b));
+            const float *stV = reinterpret_cast<const float *>(base + kPOffStV(b));
+#pragma unroll 4
+            for (int i = 0; i < kPKeys * kPHd / 4 / 128; ++i) {  // K: 8 float4 per thread
+                const int f = ct + 128 * i;
+                const int n = f >> 5, d = (f & 31) * 4;
+                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (n < nr) v = reinterpret_cast<const float4 *>(stK)[f];
+                float4 h, w;
+                h.x = tc::tf32_hi(v.x); w.x = v.x - h.x;
+                h.y = tc::tf32_hi(v.y); w.y = v.y - h.y;
+                h.z = tc::tf32_hi(v.z); w.z = v.z - h.z;
+                h.w = tc::tf32_hi(v.w); w.w = v.w - h.w;
+                const uint32_t off = tc::sw128_offset(n, d, kPKeys);
+                *reinterpret_cast<float4 *>(base + kPOffKhi(b) + off) = h;
+                *reinterpret_cast<float4 *>(base + kPOffKlo(b) + off) = w;
+            }
+            {
+                const int d = ct;  // one V^T row per thread
+#pragma unroll 4
+                for (int jg = 0; jg < kPKeys / 4; ++jg) {
+                    float x[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int n = 4 * jg + e;
+                        x[e] = (n < nr) ? stV[n * kPHd + d] : 0.f;
+                    }
+                    float4 h, w;
+                    h.x = tc::tf32_hi(x[0]); w.x = x[0] - h.x;
+                    h.y = tc::tf32_hi(x[1]); w.y = x[1] - h.y;
+                    h.z = tc::tf32_hi(x[2]); w.z = x[2] - h.z;
+                    h.w = tc::tf32_hi(x[3]); w.w = x[3] - h.w;
+                    const uint32_t off = tc::sw128_offset(d, 4 * jg, kPHd);
+                    *reinterpret_cast<float4 *>(base + kPOffVThi(b) + off) = h;
+                    *reinterpret_cast<float4 *>(base + kPOffVTlo(b) + off) = w;
+                }
+            }
+            fence_proxy_async_smem();  // operand writes -> visible to the tensor core
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&bars.st_empty[b]);
+                mbar_arrive(&bars.op_full[b]);
+            }
+        }
+        if (!ok && lane == 0) atomicExch(&s_fail, 1);
+    } else if (lane == 0) {  // warp 8
+        // ================= issuer: bulk copies and tensor-core products ========
+        auto stage = [&](int j) {
+            const int b = j & 1;
+            const int k0 = j * kPKeys;
+            const int nr = min(kPKeys, kv_end - k0);
+            const uint32_t bytes = uint32_t(nr) * kPHd * 4;
+            mbar_arrive_expect_tx(&bars.st_full[b], 2 * bytes);
+            bulk_g2s(base + kPOffStK(b), gK + size_t(k0) * kPHd, bytes, &bars.st_full[b]);
+            bulk_g2s(base + kPOffStV(b), gV + size_t(k0) * kPHd, bytes, &bars.st_full[b]);
+        };
+        const uint32_t idesc_s = tc::idesc_tf32(kPRows, kPKeys);
+        const uint32_t idesc_o = tc::idesc_tf32(kPRows, kPHd);
+        int staged = 0, s_issued = 0, pv_issued = 0;
+        for (; staged < min(2, n_kt); ++staged) stage(staged);
+        bool ok = mbar_wait(&bars.q_ready, 0);
+        auto issue_pv = [&](int j) {  // O += P(j) V(j)
+            const int b = j & 1;
+            const uint32_t scol = kPColS + 64u * b;
+#pragma unroll 1
+            for (int term = 0; term < 3; ++term) {
+                const uint32_t pcol = (term == 2) ? scol + 32 : scol;
+                const uint32_t voff = (term == 1) ? kPOffVTlo(b) : kPOffVThi(b);
+#pragma unroll
+                for (int kk = 0; kk < kPKeys / 8; ++kk) {
+                    const uint64_t bdesc = tc::sw128_kmajor_desc(sbase + voff + uint32_t(kk) * 32);
+                    tc::mma_tf32_ts(tmem + kPColO, tmem + pcol + 8 * kk, bdesc, idesc_o,
+                                    (j > 0 || term > 0 || kk > 0) ? 1u : 0u);
+                }
+            }
+            tc::commit(&bars.op_empty[b]);
+        };
+        for (int j = 0; j < n_kt && ok; ++j) {
+            const int b = j & 1;
+            // S(j) = Qhi Khi + Qhi Klo + Qlo Khi  (M 128, N 32, K 128 in 16 steps)
+            ok = mbar_wait(&bars.op_full[b], par(j));
+            if (ok && j >= 2) ok = mbar_wait(&bars.op_empty[b], par(j - 2));
+            if (!ok) break;
+            tc::fence_after_sync();
+            const uint32_t scol = kPColS + 64u * b;
+#pragma unroll 1
+            for (int term = 0; term < 3; ++term) {
+                const uint32_t qcol = (term == 2) ? kPColQlo : kPColQhi;
+                const uint32_t koff = (term == 1) ? kPOffKlo(b) : kPOffKhi(b);
+#pragma unroll
+                for (int kk = 0; kk < kPHd / 8; ++kk) {
+                    const uint64_t bdesc = tc::sw128_kmajor_desc(
+                        sbase + koff + uint32_t(kk >> 2) * (kPKeys * 128) + uint32_t(kk & 3) * 32);
+                    tc::mma_tf32_ts(tmem + scol, tmem + qcol + 8 * kk, bdesc, idesc_s,
+                                    (term > 0 || kk > 0) ? 1u : 0u);
+                }
+            }
+            tc::commit(&bars.s_full[b]);
+            ++s_issued;
+            // O += P(j-1) V(j-1) once the softmax has written P(j-1)
+            if (j >= 1) {
+                ok = mbar_wait(&bars.p_full[b ^ 1], par(j - 1));
+                if (!ok) break;
+                tc::fence_after_sync();
+                issue_pv(j - 1);
+                ++pv_issued;
+            }
+            // staging b is free once the converters took tile j from it
+            if (staged < n_kt) {
+                ok = mbar_wait(&bars.st_empty[b], par(j));
+                if (!ok) break;
+                stage(staged++);
+            }
+        }
+        if (ok) {
+            ok = mbar_wait(&bars.p_full[(n_kt - 1) & 1], par(n_kt - 1));
+            if (ok) {
+                tc::fence_after_sync();
+                issue_pv(n_kt - 1);
+                ++pv_issued;
+            }
+        }
+        if (!ok) atomicExch(&s_fail, 1);
+        // nothing may still be in flight when the CTA releases TMEM and shared
+        // memory: wait (bounded) for the last operation on every barrier
+        for (int b = 0; b < 2; ++b) {
+            const int ls = s_issued - 1 - ((s_issued - 1 - b) & 1);      // last S into b
+            if (ls >= 0) (void)mbar_wait(&bars.s_full[b], par(ls));
+            const int lp = pv_issued - 1 - ((pv_issued - 1 - b) & 1);    // last PV on b
+            if (lp >= 0) (void)mbar_wait(&bars.op_empty[b], par(lp));
+            const int lt = staged - 1 - ((staged - 1 - b) & 1);          // last copy into b
+            if (lt >= 0) (void)mbar_wait(&bars.st_full[b], par(lt));
+        }
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    if (tid == 0 && s_fail) report_error(a.err, kDevWaitTimeout);
+    if (warp == 0) tc::dealloc(tmem, kPTmemCols);
+}
+
+template <int G>
+int launch_pipe_g(leap_ctx *c, const PArgs &a) {
+    static bool attr_set[kMaxDevices] = {};
+    if (!attr_set[c->device]) {
+        const cudaError_t e = cudaFuncSetAttribute(
+            prefill_tc_pipe_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kPSmem));
+        if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(prefill_tc_pipe)");
+        attr_set[c->device] = true;
+    }
+    constexpr int BT = kPRows / G;
+    dim3 grid((a.n_tok + BT - 1) / BT, c->n_kv);
+    prefill_tc_pipe_kernel<G><<<grid, kPThreads, kPSmem, c->stream>>>(a);
+    return cuda_status(cudaGetLastError(), "prefill_tc_pipe_kernel launch");
+}
+
+}  // namespace
+
+int launch_prefill_tc_pipe(leap_ctx *c, const float *qrot, const float *kc, const float *vc,
+                           float *out, int pos0, int n_tok) {
+    if (c->hd != kPHd) {
+        set_error("tensor-core prefill handles head_dim 128");
+        return LEAP_ERR_INVALID;
+    }
+    PArgs a;
+    a.qrot = qrot;
+    a.kc = kc;
+    a.vc = vc;
+    a.head_stride = c->head_stride;
+    a.out = out;
+    a.err = c->d_err;
+    a.pos0 = pos0;
+    a.n_tok = n_tok;
+    a.n_heads = c->n_heads;
+    a.scale_log2 = kLog2e / sqrtf(float(kPHd));
+    switch (c->group) {
+        case 1: return launch_pipe_g<1>(c, a);
+        case 2: return launch_pipe_g<2>(c, a);
+        case 4: return launch_pipe_g<4>(c, a);
+        case 8: return launch_pipe_g<8>(c, a);
+        default:
+            set_error("unsupported kv_mul %d", c->group);
+            return LEAP_ERR_INVALID;
+    }
+}
+
+}  // namespace leap
