@@ -139,6 +139,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const TcArgs 
     int tiles_issued = 1, tiles_done = 0, s_issued = 0, s_done = 0, o_issued = 0, o_done = 0;
     const uint32_t idesc_s = tc::idesc_tf32(kTcRows, kTcKeys);
     const uint32_t idesc_o = tc::idesc_tf32(kTcRows, kTcHd);
+    const uint64_t dkhi = tc::sw128_kmajor_desc(sbase + kOffKhi);
+    const uint64_t dklo = tc::sw128_kmajor_desc(sbase + kOffKlo);
+    const uint64_t dvhi = tc::sw128_kmajor_desc(sbase + kOffVThi);
+    const uint64_t dvlo = tc::sw128_kmajor_desc(sbase + kOffVTlo);
 
 #pragma unroll 1
     for (int j = 0; j < n_kt; ++j) {
@@ -196,23 +200,26 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const TcArgs 
         if (j + 1 < n_kt) ++tiles_issued;
         ++s_issued;
 
-        if (tid == 0) {
+        if (warp == 0) {
             tc::fence_after_sync();
-            if (j + 1 < n_kt) issue_tile(j + 1);  // staging is free again
-            // S = Qhi Khi + Qhi Klo + Qlo Khi   (M 128, N 64, K 128 in 16 steps)
-#pragma unroll 1
-            for (int term = 0; term < 3; ++term) {
-                const uint32_t qcol = (term == 2) ? kColQlo : kColQhi;
-                const uint32_t koff = (term == 1) ? kOffKlo : kOffKhi;
+            if (tc::elect_one_sync()) {
+                if (j + 1 < n_kt) issue_tile(j + 1);  // staging is free again
+                // S = Qhi Khi + Qhi Klo + Qlo Khi   (M 128, N 64, K 128 in 16 steps)
 #pragma unroll
-                for (int kk = 0; kk < kTcHd / 8; ++kk) {
-                    const uint64_t bdesc = tc::sw128_kmajor_desc(
-                        sbase + koff + uint32_t(kk >> 2) * (kTcKeys * 128) + uint32_t(kk & 3) * 32);
-                    tc::mma_tf32_ts(tmem + kColS, tmem + qcol + 8 * kk, bdesc, idesc_s,
-                                    (term > 0 || kk > 0) ? 1u : 0u);
+                for (int term = 0; term < 3; ++term) {
+#pragma unroll
+                    for (int kk = 0; kk < kTcHd / 8; ++kk) {
+                        const uint64_t bdesc =
+                            (term == 1 ? dklo : dkhi) +
+                            uint64_t(((kk >> 2) * (kTcKeys * 128) + (kk & 3) * 32) >> 4);
+                        tc::mma_tf32_ts(tmem + kColS,
+                                        tmem + (term == 2 ? kColQlo : kColQhi) + 8 * kk, bdesc,
+                                        idesc_s, (term > 0 || kk > 0) ? 1u : 0u);
+                    }
                 }
+                tc::commit(&s_bar);
             }
-            tc::commit(&s_bar);
+            __syncwarp();
         }
 
         // ---- online softmax of this thread's row -----------------------------
@@ -274,22 +281,25 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const TcArgs 
         __syncthreads();
         ++o_issued;
 
-        if (tid == 0) {
+        if (warp == 0) {
             tc::fence_after_sync();
-            // O += Phi VThi + Phi VTlo + Plo VThi   (M 128, N 128, K 64 in 8 steps)
-#pragma unroll 1
-            for (int term = 0; term < 3; ++term) {
-                const uint32_t pcol = (term == 2) ? kColPlo : kColS;
-                const uint32_t voff = (term == 1) ? kOffVTlo : kOffVThi;
+            if (tc::elect_one_sync()) {
+                // O += Phi VThi + Phi VTlo + Plo VThi   (M 128, N 128, K 64 in 8 steps)
 #pragma unroll
-                for (int kk = 0; kk < kTcKeys / 8; ++kk) {
-                    const uint64_t bdesc = tc::sw128_kmajor_desc(
-                        sbase + voff + uint32_t(kk >> 2) * (kTcHd * 128) + uint32_t(kk & 3) * 32);
-                    tc::mma_tf32_ts(tmem + kColO, tmem + pcol + 8 * kk, bdesc, idesc_o,
-                                    (j > 0 || term > 0 || kk > 0) ? 1u : 0u);
+                for (int term = 0; term < 3; ++term) {
+#pragma unroll
+                    for (int kk = 0; kk < kTcKeys / 8; ++kk) {
+                        const uint64_t bdesc =
+                            (term == 1 ? dvlo : dvhi) +
+                            uint64_t(((kk >> 2) * (kTcHd * 128) + (kk & 3) * 32) >> 4);
+                        tc::mma_tf32_ts(tmem + kColO,
+                                        tmem + (term == 2 ? kColPlo : kColS) + 8 * kk, bdesc,
+                                        idesc_o, (j > 0 || term > 0 || kk > 0) ? 1u : 0u);
+                    }
                 }
+                tc::commit(&o_bar);
             }
-            tc::commit(&o_bar);
+            __syncwarp();
         }
     }
 

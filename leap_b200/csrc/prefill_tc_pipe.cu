@@ -12,7 +12,7 @@
 //   warps 4-7  (128 threads): convert the FP32 K/V tile j+2 staged by bulk
 //              copies into TF32 hi/lo operand tiles (K-major, 128-byte
 //              swizzle; V transposed);
-//   warp 8     (lane 0): issue the bulk copies and every tcgen05.mma:
+//   warp 8     (one elected lane): issue the bulk copies and every tcgen05.mma:
 //              S(j+1) = Q K(j+1)^T is computed while the softmax works on
 //              S(j), then O += P(j) V(j).
 //
@@ -283,63 +283,81 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_tc_pipe_kernel(const PAr
             }
         }
         if (!ok && lane == 0) atomicExch(&s_fail, 1);
-    } else if (lane == 0) {  // warp 8
+    } else {  // warp 8
         // ================= issuer: bulk copies and tensor-core products ========
+        // The whole warp runs the schedule (waits are warp-uniform); one
+        // elected lane issues, with descriptors precomputed per buffer.
+        const bool leader = tc::elect_one_sync();
+        auto wait_all = [&](uint64_t *bar, uint32_t parity) {
+            return __all_sync(0xffffffffu, mbar_wait(bar, parity));
+        };
         auto stage = [&](int j) {
             const int b = j & 1;
             const int k0 = j * kPKeys;
             const int nr = min(kPKeys, kv_end - k0);
             const uint32_t bytes = uint32_t(nr) * kPHd * 4;
-            mbar_arrive_expect_tx(&bars.st_full[b], 2 * bytes);
-            bulk_g2s(base + kPOffStK(b), gK + size_t(k0) * kPHd, bytes, &bars.st_full[b]);
-            bulk_g2s(base + kPOffStV(b), gV + size_t(k0) * kPHd, bytes, &bars.st_full[b]);
+            if (leader) {
+                mbar_arrive_expect_tx(&bars.st_full[b], 2 * bytes);
+                bulk_g2s(base + kPOffStK(b), gK + size_t(k0) * kPHd, bytes, &bars.st_full[b]);
+                bulk_g2s(base + kPOffStV(b), gV + size_t(k0) * kPHd, bytes, &bars.st_full[b]);
+            }
+            __syncwarp();
         };
         const uint32_t idesc_s = tc::idesc_tf32(kPRows, kPKeys);
         const uint32_t idesc_o = tc::idesc_tf32(kPRows, kPHd);
+        const uint64_t dkhi[2] = {tc::sw128_kmajor_desc(sbase + kPOffKhi(0)),
+                                  tc::sw128_kmajor_desc(sbase + kPOffKhi(1))};
+        const uint64_t dvhi[2] = {tc::sw128_kmajor_desc(sbase + kPOffVThi(0)),
+                                  tc::sw128_kmajor_desc(sbase + kPOffVThi(1))};
+        constexpr uint64_t kLoStep = kPOpBytes >> 4;  // hi -> lo tile of the same buffer
         int staged = 0, s_issued = 0, pv_issued = 0;
         for (; staged < min(2, n_kt); ++staged) stage(staged);
-        bool ok = mbar_wait(&bars.q_ready, 0);
+        bool ok = wait_all(&bars.q_ready, 0);
         auto issue_pv = [&](int j) {  // O += P(j) V(j)
             const int b = j & 1;
             const uint32_t scol = kPColS + 64u * b;
-#pragma unroll 1
-            for (int term = 0; term < 3; ++term) {
-                const uint32_t pcol = (term == 2) ? scol + 32 : scol;
-                const uint32_t voff = (term == 1) ? kPOffVTlo(b) : kPOffVThi(b);
+            const uint64_t dv = b ? dvhi[1] : dvhi[0];
+            if (leader) {
 #pragma unroll
-                for (int kk = 0; kk < kPKeys / 8; ++kk) {
-                    const uint64_t bdesc = tc::sw128_kmajor_desc(sbase + voff + uint32_t(kk) * 32);
-                    tc::mma_tf32_ts(tmem + kPColO, tmem + pcol + 8 * kk, bdesc, idesc_o,
-                                    (j > 0 || term > 0 || kk > 0) ? 1u : 0u);
+                for (int term = 0; term < 3; ++term) {
+#pragma unroll
+                    for (int kk = 0; kk < kPKeys / 8; ++kk) {
+                        const uint64_t bdesc = dv + (term == 1 ? kLoStep : 0) + uint64_t(kk * 2);
+                        tc::mma_tf32_ts(tmem + kPColO, tmem + scol + (term == 2 ? 32 : 0) + 8 * kk,
+                                        bdesc, idesc_o, (j > 0 || term > 0 || kk > 0) ? 1u : 0u);
+                    }
                 }
+                tc::commit(&bars.op_empty[b]);
             }
-            tc::commit(&bars.op_empty[b]);
+            __syncwarp();
         };
         for (int j = 0; j < n_kt && ok; ++j) {
             const int b = j & 1;
             // S(j) = Qhi Khi + Qhi Klo + Qlo Khi  (M 128, N 32, K 128 in 16 steps)
-            ok = mbar_wait(&bars.op_full[b], par(j));
-            if (ok && j >= 2) ok = mbar_wait(&bars.op_empty[b], par(j - 2));
+            ok = wait_all(&bars.op_full[b], par(j));
+            if (ok && j >= 2) ok = wait_all(&bars.op_empty[b], par(j - 2));
             if (!ok) break;
             tc::fence_after_sync();
             const uint32_t scol = kPColS + 64u * b;
-#pragma unroll 1
-            for (int term = 0; term < 3; ++term) {
-                const uint32_t qcol = (term == 2) ? kPColQlo : kPColQhi;
-                const uint32_t koff = (term == 1) ? kPOffKlo(b) : kPOffKhi(b);
+            const uint64_t dk = b ? dkhi[1] : dkhi[0];
+            if (leader) {
 #pragma unroll
-                for (int kk = 0; kk < kPHd / 8; ++kk) {
-                    const uint64_t bdesc = tc::sw128_kmajor_desc(
-                        sbase + koff + uint32_t(kk >> 2) * (kPKeys * 128) + uint32_t(kk & 3) * 32);
-                    tc::mma_tf32_ts(tmem + scol, tmem + qcol + 8 * kk, bdesc, idesc_s,
-                                    (term > 0 || kk > 0) ? 1u : 0u);
+                for (int term = 0; term < 3; ++term) {
+#pragma unroll
+                    for (int kk = 0; kk < kPHd / 8; ++kk) {
+                        const uint64_t bdesc = dk + (term == 1 ? kLoStep : 0) +
+                                               uint64_t(((kk >> 2) * (kPKeys * 128) + (kk & 3) * 32) >> 4);
+                        tc::mma_tf32_ts(tmem + scol, tmem + (term == 2 ? kPColQlo : kPColQhi) + 8 * kk,
+                                        bdesc, idesc_s, (term > 0 || kk > 0) ? 1u : 0u);
+                    }
                 }
+                tc::commit(&bars.s_full[b]);
             }
-            tc::commit(&bars.s_full[b]);
+            __syncwarp();
             ++s_issued;
             // O += P(j-1) V(j-1) once the softmax has written P(j-1)
             if (j >= 1) {
-                ok = mbar_wait(&bars.p_full[b ^ 1], par(j - 1));
+                ok = wait_all(&bars.p_full[b ^ 1], par(j - 1));
                 if (!ok) break;
                 tc::fence_after_sync();
                 issue_pv(j - 1);
@@ -347,20 +365,20 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_tc_pipe_kernel(const PAr
             }
             // staging b is free once the converters took tile j from it
             if (staged < n_kt) {
-                ok = mbar_wait(&bars.st_empty[b], par(j));
+                ok = wait_all(&bars.st_empty[b], par(j));
                 if (!ok) break;
                 stage(staged++);
             }
         }
         if (ok) {
-            ok = mbar_wait(&bars.p_full[(n_kt - 1) & 1], par(n_kt - 1));
+            ok = wait_all(&bars.p_full[(n_kt - 1) & 1], par(n_kt - 1));
             if (ok) {
                 tc::fence_after_sync();
                 issue_pv(n_kt - 1);
                 ++pv_issued;
             }
         }
-        if (!ok) atomicExch(&s_fail, 1);
+        if (!ok && leader) atomicExch(&s_fail, 1);
         // nothing may still be in flight when the CTA releases TMEM and shared
         // memory: wait (bounded) for the last operation on every barrier
         for (int b = 0; b < 2; ++b) {

@@ -30,6 +30,21 @@ __device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t smem_byte_addr) {
     return d;
 }
 
+// The start-address field is the low 14 bits and every shared-memory
+// address is below 256 KB, so desc(addr + off) == desc(addr) + (off >> 4):
+// descriptors of one tile are a base plus compile-time constants.
+
+// One lane of a converged warp (elect.sync): the MMA issuer.  Issuing from
+// a warp-uniform branch with descriptors precomputed keeps the issue cost
+// per tcgen05.mma near the tensor core's own time even for small N.
+__device__ __forceinline__ bool elect_one_sync() {
+    uint32_t p = 0;
+    asm volatile(
+        "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\tselp.u32 %0, 1, 0, e;\n\t}"
+        : "=r"(p));
+    return p != 0;
+}
+
 // 32-bit instruction descriptor for kind::tf32, F32 accumulate, both
 // operands K-major, dense.
 //   bits 4-5 D format (1 = F32); 7-9 A format, 10-12 B format (2 = TF32);
