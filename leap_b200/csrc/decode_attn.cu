@@ -592,7 +592,6 @@ int launch_t(leap_ctx *c, const DecodeArgs &a, const DecodeSeq &tab, int total_s
 int plan_decode(const leap_ctx *c, DecodeSeq &tab, int shape) {
     const int tile_bytes = shape == 1 ? 32768 : 16384;
     const int per_sm = shape == 1 ? 1 : 2;
-    const int tile = tile_bytes / (c->hd * 4);
     const long cap_rows = 16L * tile_bytes / (c->hd * 4 * 2);  // 256/512 KB of K+V per CTA
     long total = 0;
     int max_ctx = 0;
@@ -607,7 +606,16 @@ int plan_decode(const leap_ctx *c, DecodeSeq &tab, int shape) {
     if (chunk > cap_rows) chunk = cap_rows;
     const long min_chunk = (max_ctx + kMaxSplitsPerSeq - 1) / kMaxSplitsPerSeq;
     if (chunk < min_chunk) chunk = min_chunk;
-    chunk = (chunk + tile - 1) / tile * tile;
+    // Chunks are whole 8-row groups (a CTA's last tile may be partial).  When
+    // the work fits one wave, grow the chunk until the per-sequence ceilings
+    // no longer push the CTA count past it.
+    chunk = (chunk + 7) / 8 * 8;
+    auto n_ctas = [&](long ch) {
+        long n = 0;
+        for (int i = 0; i < tab.n_seq; ++i) n += (tab.pos[i] + ch) / ch;
+        return n * c->n_kv;
+    };
+    while (chunk < cap_rows && n_ctas(chunk) > target) chunk += 8;
     tab.chunk = int(chunk);
     int acc = 0;
     for (int i = 0; i < tab.n_seq; ++i) {
