@@ -467,8 +467,8 @@ def run_prefill(args):
             "ms_per_step": round(ms, 4), "higher_is_better": True, "dtype": "f32 (3xTF32)"
             if args.prefill_impl != 1 else "f32",
             "config": {"workload": f"config4: causal prefill L={L}, Llama-3-8B heads, batch 1",
-                       "seq_len": L, "impl": {0: "tcgen05 3xTF32", 1: "CUDA-core FP32",
-                                2: "tcgen05 3xTF32 pipelined"}[args.prefill_impl]},
+                       "seq_len": L, "impl": {0: "tcgen05 3xTF32 pipelined", 1: "CUDA-core FP32",
+                                2: "tcgen05 3xTF32 serial"}[args.prefill_impl]},
             "roofline": {"bound": "tensor", "achieved": round(tflops, 2),
                          "tensor_tflops_issued": round(3 * tflops, 2)
                          if args.prefill_impl != 1 else None,
@@ -808,7 +808,7 @@ def main():
     ap.add_argument("--prefill", type=int, default=0,
                     help="benchmark config 4 (causal prefill of this many tokens) instead")
     ap.add_argument("--prefill-impl", type=int, default=0,
-                    help="0 tcgen05 3xTF32, 1 CUDA-core FP32, 2 tcgen05 3xTF32 pipelined")
+                    help="0 tcgen05 3xTF32 pipelined, 1 CUDA-core FP32, 2 tcgen05 3xTF32 serial")
     ap.add_argument("--layers", type=int, default=N_LAYERS)
     ap.add_argument("--ctx", type=int, default=CTX)
     ap.add_argument("--batched", action="store_true",

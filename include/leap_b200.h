@@ -332,8 +332,10 @@ LEAP_API int leap_engine_prefill(leap_engine *e, const int *tokens, int n,
                                  int pos0, int *next_token);
 
 /* Prefill kernel selection (for tests and benchmarks):
- *   0 = default (tensor-core 3xTF32 path), 1 = CUDA-core FP32 path,
- *   2 = tensor-core 3xTF32, software-pipelined across warp roles. */
+ *   0 = default: tensor-core 3xTF32, software-pipelined across warp roles
+ *       (softmax, operand conversion and MMA issue overlap),
+ *   1 = CUDA-core FP32 path,
+ *   2 = tensor-core 3xTF32, one tile at a time (no overlap). */
 LEAP_API int leap_set_prefill_impl(leap_ctx *ctx, int impl);
 
 /* ---- support ops of the layer, one kernel each --------------------------

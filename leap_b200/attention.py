@@ -213,6 +213,7 @@ class AttentionContext:
         check(lib().leap_set_overlap(self.handle, int(bool(enable))))
 
     def set_prefill_impl(self, impl: int) -> None:
-        """0 = tensor-core 3xTF32 kernel, 1 = CUDA-core FP32 kernel,
-        2 = tensor-core 3xTF32 kernel pipelined across warp roles."""
+        """0 = tensor-core 3xTF32 kernel pipelined across warp roles (default),
+        1 = CUDA-core FP32 kernel, 2 = tensor-core 3xTF32 kernel, one tile at
+        a time."""
         check(lib().leap_set_prefill_impl(self.handle, impl))

@@ -247,7 +247,8 @@ int launch_fma(leap_ctx *c, const float *qrot, const float *kc, const float *vc,
 // is not supported there.
 int launch_prefill_tc(leap_ctx *c, const float *qrot, const float *kc, const float *vc,
                       float *out, int pos0, int n_tok);
-// the same product, software-pipelined across warp roles (prefill_tc_pipe.cu)
+// the same product, software-pipelined across warp roles (prefill_tc_pipe.cu):
+// the default
 int launch_prefill_tc_pipe(leap_ctx *c, const float *qrot, const float *kc, const float *vc,
                            float *out, int pos0, int n_tok);
 
@@ -277,7 +278,7 @@ int launch_prefill(leap_ctx *c, int slot, int layer, int pos0, int n_tok, const 
     if (int st = cuda_status(cudaGetLastError(), "prefill_rope_append launch")) return st;
 
     if (c->prefill_impl == 0 || c->prefill_impl == 2) {
-        const int st = c->prefill_impl == 2
+        const int st = c->prefill_impl == 0
                            ? launch_prefill_tc_pipe(c, c->d_qrot, kc, vc, out, pos0, n_tok)
                            : launch_prefill_tc(c, c->d_qrot, kc, vc, out, pos0, n_tok);
         if (st != LEAP_ERR_INVALID) return st;

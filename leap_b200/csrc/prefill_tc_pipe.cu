@@ -9,10 +9,10 @@
 //
 //   warps 0-3  (128 threads, TMEM lanes = the CTA's 128 query rows): online
 //              softmax of S(j) in FP32 registers, P(j) hi/lo back to TMEM;
-//   warps 4-7  (128 threads): convert the FP32 K/V tile j+2 staged by bulk
+//   warps 4-11 (256 threads): convert the FP32 K/V tile j+2 staged by bulk
 //              copies into TF32 hi/lo operand tiles (K-major, 128-byte
 //              swizzle; V transposed);
-//   warp 8     (one elected lane): issue the bulk copies and every tcgen05.mma:
+//   warp 12    (one elected lane): issue the bulk copies and every tcgen05.mma:
 //              S(j+1) = Q K(j+1)^T is computed while the softmax works on
 //              S(j), then O += P(j) V(j).
 //
@@ -35,7 +35,8 @@ namespace {
 constexpr int kPRows = 128;                  // query rows per CTA = TMEM lanes
 constexpr int kPKeys = 32;                   // keys per tile
 constexpr int kPHd = 128;
-constexpr int kPThreads = 288;               // 4 softmax + 4 convert + 1 issue warps
+constexpr int kPConv = 8;                    // converter warps
+constexpr int kPThreads = 32 * (4 + kPConv + 1);  // softmax, convert, issue warps
 constexpr uint32_t kPColQhi = 0, kPColQlo = 128, kPColO = 256, kPColS = 384;
 constexpr uint32_t kPTmemCols = 512;
 constexpr float kPMaxLag = 8.0f;
@@ -98,8 +99,8 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_tc_pipe_kernel(const PAr
         mbar_init(&bars.q_ready, 4);
         for (int b = 0; b < 2; ++b) {
             mbar_init(&bars.st_full[b], 1);
-            mbar_init(&bars.st_empty[b], 4);
-            mbar_init(&bars.op_full[b], 4);
+            mbar_init(&bars.st_empty[b], kPConv);
+            mbar_init(&bars.op_full[b], kPConv);
             mbar_init(&bars.op_empty[b], 1);
             mbar_init(&bars.s_full[b], 1);
             mbar_init(&bars.p_full[b], 4);
@@ -227,9 +228,9 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_tc_pipe_kernel(const PAr
         } else if (lane == 0) {
             atomicExch(&s_fail, 1);
         }
-    } else if (warp < 8) {
+    } else if (warp < 4 + kPConv) {
         // ================= converter warps: staging -> TF32 hi/lo operands ======
-        const int ct = tid - 128;  // 0..127
+        const int ct = tid - 128;  // 0 .. 32*kPConv-1
         bool ok = true;
         for (int j = 0; j < n_kt && ok; ++j) {
             const int b = j & 1;
@@ -240,9 +241,9 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_tc_pipe_kernel(const PAr
             if (!ok) break;
             const float *stK = reinterpret_cast<const float *>(base + kPOffStK(b));
             const float *stV = reinterpret_cast<const float *>(base + kPOffStV(b));
-#pragma unroll 4
-            for (int i = 0; i < kPKeys * kPHd / 4 / 128; ++i) {  // K: 8 float4 per thread
-                const int f = ct + 128 * i;
+#pragma unroll
+            for (int i = 0; i < kPKeys * kPHd / 4 / (32 * kPConv); ++i) {  // K: float4s
+                const int f = ct + 32 * kPConv * i;
                 const int n = f >> 5, d = (f & 31) * 4;
                 float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
                 if (n < nr) v = reinterpret_cast<const float4 *>(stK)[f];
@@ -256,9 +257,13 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_tc_pipe_kernel(const PAr
                 *reinterpret_cast<float4 *>(base + kPOffKlo(b) + off) = w;
             }
             {
-                const int d = ct;  // one V^T row per thread
-#pragma unroll 4
-                for (int jg = 0; jg < kPKeys / 4; ++jg) {
+                // V^T row d, a 1/kVParts share of its keys per thread
+                constexpr int kVParts = 32 * kPConv / kPHd;
+                constexpr int kVGroups = kPKeys / 4 / kVParts;
+                const int d = ct % kPHd;
+                const int jg0 = (ct / kPHd) * kVGroups;
+#pragma unroll
+                for (int jg = jg0; jg < jg0 + kVGroups; ++jg) {
                     float x[4];
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
@@ -283,7 +288,7 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_tc_pipe_kernel(const PAr
             }
         }
         if (!ok && lane == 0) atomicExch(&s_fail, 1);
-    } else {  // warp 8
+    } else {  // warp 4 + kPConv
         // ================= issuer: bulk copies and tensor-core products ========
         // The whole warp runs the schedule (waits are warp-uniform); one
         // elected lane issues, with descriptors precomputed per buffer.
@@ -313,6 +318,25 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_tc_pipe_kernel(const PAr
         int staged = 0, s_issued = 0, pv_issued = 0;
         for (; staged < min(2, n_kt); ++staged) stage(staged);
         bool ok = wait_all(&bars.q_ready, 0);
+        auto issue_s = [&](int j) {  // S(j) = Qhi Khi + Qhi Klo + Qlo Khi  (M 128, N 32, K 128)
+            const int b = j & 1;
+            const uint32_t scol = kPColS + 64u * b;
+            const uint64_t dk = b ? dkhi[1] : dkhi[0];
+            if (leader) {
+#pragma unroll
+                for (int term = 0; term < 3; ++term) {
+#pragma unroll
+                    for (int kk = 0; kk < kPHd / 8; ++kk) {
+                        const uint64_t bdesc = dk + (term == 1 ? kLoStep : 0) +
+                                               uint64_t(((kk >> 2) * (kPKeys * 128) + (kk & 3) * 32) >> 4);
+                        tc::mma_tf32_ts(tmem + scol, tmem + (term == 2 ? kPColQlo : kPColQhi) + 8 * kk,
+                                        bdesc, idesc_s, (term > 0 || kk > 0) ? 1u : 0u);
+                    }
+                }
+                tc::commit(&bars.s_full[b]);
+            }
+            __syncwarp();
+        };
         auto issue_pv = [&](int j) {  // O += P(j) V(j)
             const int b = j & 1;
             const uint32_t scol = kPColS + 64u * b;
@@ -331,51 +355,50 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_tc_pipe_kernel(const PAr
             }
             __syncwarp();
         };
-        for (int j = 0; j < n_kt && ok; ++j) {
-            const int b = j & 1;
-            // S(j) = Qhi Khi + Qhi Klo + Qlo Khi  (M 128, N 32, K 128 in 16 steps)
-            ok = wait_all(&bars.op_full[b], par(j));
-            if (ok && j >= 2) ok = wait_all(&bars.op_empty[b], par(j - 2));
-            if (!ok) break;
-            tc::fence_after_sync();
-            const uint32_t scol = kPColS + 64u * b;
-            const uint64_t dk = b ? dkhi[1] : dkhi[0];
-            if (leader) {
-#pragma unroll
-                for (int term = 0; term < 3; ++term) {
-#pragma unroll
-                    for (int kk = 0; kk < kPHd / 8; ++kk) {
-                        const uint64_t bdesc = dk + (term == 1 ? kLoStep : 0) +
-                                               uint64_t(((kk >> 2) * (kPKeys * 128) + (kk & 3) * 32) >> 4);
-                        tc::mma_tf32_ts(tmem + scol, tmem + (term == 2 ? kPColQlo : kPColQhi) + 8 * kk,
-                                        bdesc, idesc_s, (term > 0 || kk > 0) ? 1u : 0u);
-                    }
+        // Issue whichever step is ready: S(j) once tile j's operands are
+        // converted and PV(j-2) has released S/P buffer j%2; PV(j) once the
+        // softmax has written P(j); the copy of tile j+2 once the converters
+        // have taken tile j from staging.  Every test is of the next phase of
+        // its barrier only (the one before it was observed), so parities
+        // cannot alias.  No progress for kMaxWaitNs ends the loop.
+        unsigned long long t_idle = global_ns();
+        uint32_t idle_polls = 0;
+        while (ok && pv_issued < n_kt) {
+            bool progress = false;
+            if (s_issued < n_kt && s_issued <= pv_issued + 1) {
+                const int j = s_issued, b = j & 1;
+                bool ready = mbar_test(&bars.op_full[b], par(j));
+                if (ready && j >= 2) ready = mbar_test(&bars.op_empty[b], par(j - 2));
+                if (__all_sync(0xffffffffu, ready)) {
+                    tc::fence_after_sync();
+                    issue_s(j);
+                    ++s_issued;
+                    progress = true;
                 }
-                tc::commit(&bars.s_full[b]);
             }
-            __syncwarp();
-            ++s_issued;
-            // O += P(j-1) V(j-1) once the softmax has written P(j-1)
-            if (j >= 1) {
-                ok = wait_all(&bars.p_full[b ^ 1], par(j - 1));
-                if (!ok) break;
-                tc::fence_after_sync();
-                issue_pv(j - 1);
-                ++pv_issued;
+            if (pv_issued < s_issued) {
+                const int j = pv_issued;
+                if (__all_sync(0xffffffffu, mbar_test(&bars.p_full[j & 1], par(j)))) {
+                    tc::fence_after_sync();
+                    issue_pv(j);
+                    ++pv_issued;
+                    progress = true;
+                }
             }
-            // staging b is free once the converters took tile j from it
             if (staged < n_kt) {
-                ok = wait_all(&bars.st_empty[b], par(j));
-                if (!ok) break;
-                stage(staged++);
+                const int j = staged;
+                if (__all_sync(0xffffffffu, mbar_test(&bars.st_empty[j & 1], par(j - 2)))) {
+                    stage(j);
+                    ++staged;
+                    progress = true;
+                }
             }
-        }
-        if (ok) {
-            ok = wait_all(&bars.p_full[(n_kt - 1) & 1], par(n_kt - 1));
-            if (ok) {
-                tc::fence_after_sync();
-                issue_pv(n_kt - 1);
-                ++pv_issued;
+            if (progress) {
+                idle_polls = 0;
+            } else if ((++idle_polls & 255) == 0) {
+                const unsigned long long t = global_ns();
+                if (idle_polls == 256) t_idle = t;
+                else if (t - t_idle > kMaxWaitNs || idle_polls >= kMaxWaitPolls) ok = false;
             }
         }
         if (!ok && leader) atomicExch(&s_fail, 1);
