@@ -17,8 +17,9 @@ path).  Times are CUDA-event device times, max over ranks.
 value      : algorithmic KV-path bytes / s over all ranks (GB/s), with the
              inputs resident in HBM
 e2e        : the same through the host-pointer C ABI entry point
-             (leap_attn_decode_host): pinned staging, H2D of q/k/v, kernel,
-             D2H of the output, per layer, blocking
+             (leap_attn_decode_host, ctypes with prebound pointers): q/k/v
+             in through pinned staging, kernel, output back, per layer,
+             blocking
 roofline   : dominant kernel (decode_attn_kernel) bytes per launch / mean
              launch time, against MEASURED_PEAKS.json hbm_gbs
 cpu_baseline: the reference's own attention block (oracle/_ref, compiled
@@ -364,18 +365,31 @@ def run_gpu_arm(args):
     # ---- end to end through the host-pointer entry point -------------------
     e2e = None
     if not args.no_e2e:
-        hq = q.cpu().numpy()
-        hk = kn.cpu().numpy()
-        hv = vn.cpu().numpy()
+        # The C-ABI call an engine makes per layer (leap_attn_decode_host on
+        # host buffers it owns), bound once through ctypes: q/k/v in through
+        # pinned staging, kernel, output back, blocking.
+        from leap_b200._native import lib as _lib
+        hq = np.ascontiguousarray(q.cpu().numpy())
+        hk = np.ascontiguousarray(kn.cpu().numpy())
+        hv = np.ascontiguousarray(vn.cpu().numpy())
+        hout = np.empty((N_HEADS, HD), np.float32)
+        fn, handle = _lib().leap_attn_decode_host, ctx.handle
+        ptrs = [(hq[l].ctypes.data, hk[l].ctypes.data, hv[l].ctypes.data)
+                for l in range(n_layers)]
+        op = hout.ctypes.data
+
+        def host_step():
+            for layer in range(n_layers):
+                if fn(handle, layer, pos, *ptrs[layer], op) != 0:
+                    raise RuntimeError("leap_attn_decode_host failed")
+
         ctx.sync()
         for _ in range(min(args.warmup, 2)):
-            for layer in range(n_layers):
-                ctx.decode_host(layer, pos, hq[layer], hk[layer], hv[layer])
+            host_step()
         barrier()
         t0 = time.perf_counter()
         for _ in range(args.steps):
-            for layer in range(n_layers):
-                ctx.decode_host(layer, pos, hq[layer], hk[layer], hv[layer])
+            host_step()
         e2e_s = max_over_ranks(time.perf_counter() - t0)
         barrier()
         e2e = {"value": round(per_launch * n_layers * args.steps * world / e2e_s / 1e9, 2),

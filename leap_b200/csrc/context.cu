@@ -242,6 +242,9 @@ int leap_ctx_create(const leap_ctx_desc *d, leap_ctx **out) {
 
     const size_t sb = leap::stage_floats(c) * sizeof(float);
     if ((e = cudaMallocHost(&c->h_stage, sb)) != cudaSuccess) return fail(e, "cudaMallocHost(stage)");
+    if ((e = cudaHostGetDevicePointer(reinterpret_cast<void **>(&c->h_stage_dev), c->h_stage, 0)) !=
+        cudaSuccess)
+        return fail(e, "cudaHostGetDevicePointer(stage)");
     if ((e = cudaMalloc(&c->d_stage, sb)) != cudaSuccess) return fail(e, "cudaMalloc(stage)");
     if ((e = cudaMemset(c->d_stage, 0, sb)) != cudaSuccess) return fail(e, "cudaMemset(stage)");
     c->d_err = reinterpret_cast<int *>(c->d_stage + leap::stage_floats(c) - 4);
@@ -455,18 +458,19 @@ int leap_attn_decode_host(leap_ctx *c, int layer, int pos, const float *q, const
     std::memcpy(hq, q, nq * sizeof(float));
     std::memcpy(hk, k_new, nk * sizeof(float));
     std::memcpy(hv, v_new, nk * sizeof(float));
-    LEAP_TRY_CUDA(cudaMemcpyAsync(dq, hq, (nq + 2 * nk) * sizeof(float), cudaMemcpyHostToDevice,
-                                  c->stream),
-                  "stage in");
+    // q|k|v in, decode, out|error word back: three kernels chained by
+    // programmatic dependent launch (stage_host.cu), one synchronization
+    float *hq_dev = c->h_stage_dev, *ho_dev = hq_dev + nq + 2 * nk;
+    if (int st = leap::launch_stage_in(c->stream, hq_dev, dq, int((nq + 2 * nk) / 4))) return st;
+    // the grid before the decode is stage_in, which writes no cache row: the
+    // decode may start its K/V copies while it runs
+    c->last_written_layer = leap_ctx::kWroteNone;
     leap::DecodeSeq tab;
     tab.n_seq = 1;
     tab.pos[0] = pos;
     tab.slot[0] = 0;
     if (int st = leap::launch_decode(c, layer, tab, dq, dk, dv, dout)) return st;
-    // out and the error word come back in one copy
-    LEAP_TRY_CUDA(cudaMemcpyAsync(ho, dout, (nq + 4) * sizeof(float), cudaMemcpyDeviceToHost,
-                                  c->stream),
-                  "stage out");
+    if (int st = leap::launch_stage_out(c->stream, dout, ho_dev, int((nq + 4) / 4))) return st;
     LEAP_TRY_CUDA(cudaStreamSynchronize(c->stream), "cudaStreamSynchronize");
     int err;
     std::memcpy(&err, ho + nq, sizeof(int));

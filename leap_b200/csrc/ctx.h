@@ -42,6 +42,7 @@ struct leap_ctx {
     int overlap = 1;
     int last_written_layer = kWroteAll;  // layer the previous op wrote
     static constexpr int kWroteAll = -2;
+    static constexpr int kWroteNone = -1;  // the previous grid wrote no cache row
 
     // decode kernel choice: 0 auto, 1 split-KV (global combine),
     // 2 cluster (distributed-shared-memory combine)
@@ -53,6 +54,7 @@ struct leap_ctx {
 
     // host-pointer entry points: pinned staging and device mirrors
     float *h_stage = nullptr;  // pinned: q | k | v | out for one token
+    float *h_stage_dev = nullptr;  // the same pinned buffer as device code addresses it
     float *d_stage = nullptr;
 
     // prefill scratch (rotated q), grown on demand
@@ -108,6 +110,12 @@ int plan_decode(const leap_ctx *c, DecodeSeq &tab, int shape);
 
 // decode_cluster.cu: co-resident 16-CTA clusters, and the launch.
 int decode_cluster_capacity(leap_ctx *c, int *n);
+// Host-pointer staging kernels (stage_host.cu): n4 float4s pinned host ->
+// device after everything before on the stream, and device -> pinned host
+// once the previous grid (launched with programmatic serialization) is done.
+int launch_stage_in(cudaStream_t st, const float *h_src, float *d_dst, int n4);
+int launch_stage_out(cudaStream_t st, const float *d_src, float *h_dst, int n4);
+
 int launch_decode_cluster(leap_ctx *c, int layer, const DecodeSeq &tab, const float *q,
                           const float *k_new, const float *v_new, float *out, bool overlap);
 
