@@ -542,6 +542,9 @@ def run_model(args):
     cfg = ModelConfig(*shape)
     lb, le = stage_range(cfg.n_layers, rank, world)
     chunk = 512
+    if args.q8_gemv is not None:
+        from leap_b200._native import check as _check, lib as _lib
+        _check(_lib().leap_op_set_q8_gemv(args.q8_gemv))
     eng = Transformer.synthetic(cfg, q8, seed=SEED, device=local, rope_theta=theta,
                                 layer_range=(lb, le), max_chunk=chunk)
     eng.bind_torch_stream()
@@ -830,6 +833,9 @@ def main():
     ap.add_argument("--model", choices=sorted(MODELS), default=None,
                     help="end-to-end decode of a whole model (pipeline over the ranks)")
     ap.add_argument("--prompt", type=int, default=0, help="prompt tokens for --model")
+    ap.add_argument("--q8-gemv", type=int, default=None,
+                    help="W8A8 GEMV kernel for --model: 0 sliced, 1 register-staged, "
+                         "2 persistent bulk-copy (default: the library's, 2)")
     ap.add_argument("--comm", choices=["native", "torch"], default="native",
                     help="stage transport for --model on N > 1 ranks")
     args = ap.parse_args()

@@ -374,9 +374,11 @@ LEAP_API int leap_op_qmatmul(void *stream, float *y, const int8_t *xq,
                              const float *ws, int n, int d, int T, int gs,
                              const float *res);
 /* W8A8 GEMV kernel selection for T == 1 (process-wide; tests/benchmarks):
- * 0 = one row per lane with the row's groups sliced over lanes (default),
- * 1 = register-staged rows with 4-lane group shuffles.  Both compute the
- * same bits. */
+ * 0 = one row per lane with the row's groups sliced over lanes,
+ * 1 = register-staged rows with 4-lane group shuffles,
+ * 2 = persistent CTAs streaming 8-row x 2 KB items through a bulk-copy
+ *     pipeline, warp-specialised (dot warps, a copy producer, a chain warp;
+ *     the default).  All compute the same bits. */
 LEAP_API int leap_op_set_q8_gemv(int impl);
 /* Greedy sampling (Sampler.cpp:20-120 at temperature 0): index of the
  * first maximum in the reference's scan order. */

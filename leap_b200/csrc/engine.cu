@@ -837,11 +837,12 @@ int leap_op_qmatmul(void *stream, float *y, const int8_t *xq, const float *xs, c
 
 int leap_op_set_q8_gemv(int impl) {
     leap::clear_error();
-    if (impl != 0 && impl != 1) {
-        leap::set_error("q8 gemv impl %d (0 sliced, 1 register-staged)", impl);
+    if (impl < 0 || impl > 2) {
+        leap::set_error("q8 gemv impl %d (0 sliced, 1 register-staged, 2 persistent bulk-copy)", impl);
         return LEAP_ERR_INVALID;
     }
     leap::eng::g_q8_slice = impl == 0;
+    leap::eng::g_q8_tma = impl == 2;
     return LEAP_OK;
 }
 

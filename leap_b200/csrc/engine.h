@@ -21,6 +21,7 @@ int quantize(cudaStream_t st, int8_t *q, float *s, const float *x, size_t n, int
 int gemv_q8(cudaStream_t st, float *y, const int8_t *xq, const float *xs, const int8_t *wq,
             const float *ws, int n, int d, const float *res, int *err = nullptr);
 extern bool g_q8_slice;  // int8 GEMV: sliced one-row-per-lane kernel (else register-staged)
+extern bool g_q8_tma;    // int8 GEMV: persistent bulk-copy kernel (default; takes precedence)
 int gemm_q8(cudaStream_t st, float *y, const int8_t *xq, const float *xs, const int8_t *wq,
             const float *ws, int n, int d, int T, const float *res);
 int gemv_f32(cudaStream_t st, float *y, const float *x, const float *w, int n, int d,

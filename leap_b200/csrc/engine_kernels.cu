@@ -16,6 +16,7 @@
 // while its predecessor still runs, may read only constant data (weights)
 // before griddepcontrol.wait, and lets its own successor launch once it has
 // passed that wait.  The GEMVs use the window to start their weight stream.
+#include <algorithm>
 #include <cstdint>
 #include <mutex>
 #include <vector>
@@ -338,6 +339,179 @@ gemv_q8_slice_kernel(float *y, const int8_t *__restrict__ xq, const float *__res
         for (int g = 0; g < ng; ++g) val = fmaf(dr[g], tr[g], val);
         const int r = blockIdx.x * kSR + tid;
         y[r] = res ? __fadd_rn(res[r], val) : val;
+    }
+}
+
+// ---- W8A8 GEMV, persistent bulk-copy pipeline -------------------------------
+// Work = (block of 8 rows, 2048-byte column chunk) items, taken in order by
+// a persistent CTA (blocks blockIdx.x, +gridDim.x, ...).  An item's 8 row
+// chunks move with one 1-D bulk copy each into one of kPS stages.  Ten warps:
+//   warps 0-7  one group dot each per item (warp w = row w, lane l = group l
+//              of the chunk; the lane's four 16-byte reads are rotated so a
+//              quarter-warp touches eight bank groups) into a [row][group]
+//              table (two buffers), then release the stage;
+//   warp 8     issues the copies, each as soon as its stage is released
+//              (the first kPS before griddepcontrol.wait: weights are
+//              constant);
+//   warp 9     prefetches the next block's weight scales with cp.async and
+//              runs each row's chain
+//              val = fma(float(dot), w_s * x_s, val) through the chunk's
+//              groups in order — the reference's arithmetic — while the dot
+//              warps already work on the next item.
+// All hand-offs are mbarriers; every wait is bounded.
+constexpr int kPR = 8;                   // rows per block = dot warps
+constexpr int kPK = 2048;                // bytes of a row per item
+constexpr int kPS = 3;                   // stages
+constexpr int kPG = kPK / 64;            // groups per item = lanes
+constexpr int kPStage = kPR * kPK;       // bytes per stage
+constexpr int kPThreads = 32 * (kPR + 2);
+
+__device__ __forceinline__ void cp_async4(void *dst_smem, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(dst_smem)), "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
+__global__ void __launch_bounds__(kPThreads)
+gemv_q8_stream_kernel(float *y, const int8_t *__restrict__ xq, const float *__restrict__ xs,
+                      const int8_t *__restrict__ wq, const float *__restrict__ ws, int n, int d,
+                      const float *res, int *err) {
+    extern __shared__ __align__(128) unsigned char psm[];
+    const int ng = n >> 6;
+    unsigned char *stg = psm;                                    // [kPS][kPR][kPK]
+    int4 *sx = reinterpret_cast<int4 *>(psm + kPS * kPStage);     // [n / 16]
+    float *sxs = reinterpret_cast<float *>(sx + (n >> 4));       // [ng]
+    float *sws = sxs + ng;                                       // [2][kPR][ng]
+    __shared__ uint64_t full[kPS], empty[kPS], ready[2], done[2];
+    __shared__ float tab[2][kPR][kPG + 1];
+    __shared__ int issued, failed;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int nblocks = (d + kPR - 1) / kPR;
+    const int nchunks = (n + kPK - 1) / kPK;
+    const int my_blocks = blockIdx.x < nblocks ? (nblocks - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    const int items = my_blocks * nchunks;
+    auto block_of = [&](int k) { return blockIdx.x + k * gridDim.x; };
+    auto rows_of = [&](int rb) { return min(kPR, d - rb * kPR); };
+    auto issue = [&](int it) {  // producer warp: item `it` into stage it % kPS
+        const int s = it % kPS, rb = block_of(it / nchunks), c = it % nchunks;
+        const int k0 = c * kPK, nr = rows_of(rb);
+        const uint32_t kb = uint32_t(min(kPK, n - k0));
+        if (lane == 0) mbar_arrive_expect_tx(&full[s], kb * uint32_t(nr));
+        __syncwarp();
+        if (lane < nr)
+            bulk_g2s(stg + s * kPStage + lane * kPK, wq + size_t(rb * kPR + lane) * n + k0, kb,
+                     &full[s]);
+        if (lane == 0) issued = it + 1;
+    };
+    auto fetch_scales = [&](int k) {  // chain warp: block k's weight scales -> sws[k & 1]
+        if (k >= my_blocks) return;
+        const int rb = block_of(k);
+        const float *src = ws + size_t(rb) * kPR * ng;
+        float *dst = sws + (k & 1) * kPR * ng;
+        for (int i = lane; i < rows_of(rb) * ng; i += 32) cp_async4(dst + i, src + i);
+    };
+    if (tid == 0) {
+        for (int s = 0; s < kPS; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kPR);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&ready[b], kPR);
+            mbar_init(&done[b], 1);
+        }
+        issued = 0;
+        failed = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (warp == kPR)
+        for (int it = 0; it < min(kPS, items); ++it) issue(it);
+    if (warp == kPR + 1) fetch_scales(0);
+    pdl_enter();
+    for (int i = tid; i < (n >> 4); i += blockDim.x) sx[i] = reinterpret_cast<const int4 *>(xq)[i];
+    for (int g = tid; g < ng; g += blockDim.x) sxs[g] = xs[g];
+    __syncthreads();
+
+    if (warp < kPR) {
+        // ---- dot warps ------------------------------------------------------
+        const int rot = (lane >> 1) & 3;
+        for (int it = 0; it < items; ++it) {
+            const int s = it % kPS, b = it & 1, c = it % nchunks;
+            const int gcount = min(kPK, n - c * kPK) >> 6;
+            bool ok = mbar_wait(&full[s], uint32_t(it / kPS) & 1u);
+            if (ok && it >= 2) ok = mbar_wait(&done[b], uint32_t((it - 2) >> 1) & 1u);
+            if (!__all_sync(0xffffffffu, ok)) {
+                if (lane == 0) atomicExch(&failed, 1);
+                break;
+            }
+            if (lane < gcount) {
+                const int4 *wr = reinterpret_cast<const int4 *>(stg + s * kPStage + warp * kPK + lane * 64);
+                const int4 *xr = sx + (c * kPG + lane) * 4;
+                int dot = 0;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int cc = (j + rot) & 3;
+                    const int4 wv = wr[cc], xv = xr[cc];
+                    dot = __dp4a(wv.x, xv.x, dot);
+                    dot = __dp4a(wv.y, xv.y, dot);
+                    dot = __dp4a(wv.z, xv.z, dot);
+                    dot = __dp4a(wv.w, xv.w, dot);
+                }
+                tab[b][warp][lane] = float(dot);
+            }
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&empty[s]);
+                mbar_arrive(&ready[b]);
+            }
+        }
+    } else if (warp == kPR) {
+        // ---- producer: refill each stage as soon as the dot warps release it
+        bool ok = true;
+        for (int it = kPS; it < items && ok; ++it) {
+            ok = __all_sync(0xffffffffu,
+                            mbar_wait(&empty[it % kPS], uint32_t((it - kPS) / kPS) & 1u));
+            if (ok) issue(it);
+        }
+        if (!ok && lane == 0) atomicExch(&failed, 1);
+    } else {
+        // ---- chains ---------------------------------------------------------
+        int it = 0;
+        bool ok = true;
+        for (int k = 0; k < my_blocks && ok; ++k) {
+            const int rb = block_of(k), nr = rows_of(rb);
+            cp_async_wait_all();  // this block's scales (issued a block ago)
+            __syncwarp();
+            fetch_scales(k + 1);
+            const float *wsr = sws + (k & 1) * kPR * ng + lane * ng;
+            float val = 0.f;
+            for (int c = 0; c < nchunks; ++c, ++it) {
+                const int b = it & 1, g0 = c * kPG;
+                const int gcount = min(kPK, n - c * kPK) >> 6;
+                ok = __all_sync(0xffffffffu, mbar_wait(&ready[b], uint32_t(it >> 1) & 1u));
+                if (!ok) break;
+                if (lane < nr)
+                    for (int g = 0; g < gcount; ++g)
+                        val = fmaf(tab[b][lane][g], __fmul_rn(wsr[g0 + g], sxs[g0 + g]), val);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&done[b]);
+            }
+            if (ok && lane < nr) {
+                const int r = rb * kPR + lane;
+                y[r] = res ? __fadd_rn(res[r], val) : val;
+            }
+        }
+        cp_async_wait_all();
+        if (!ok && lane == 0) atomicExch(&failed, 1);
+    }
+    __syncthreads();
+    if (failed) {
+        // a wait gave up: let the copies in flight land, then report
+        for (int i2 = max(0, issued - kPS); i2 < issued; ++i2)
+            (void)mbar_wait(&full[i2 % kPS], uint32_t(i2 / kPS) & 1u);
+        if (tid == 0) report_error(err, kDevWaitTimeout);
     }
 }
 
@@ -746,6 +920,30 @@ int set_smem_attr(const void *fn, bool *done, size_t bytes, const char *what) {
 constexpr size_t kGemvSmemMax = 200 * 1024;
 
 bool g_q8_slice = true;
+bool g_q8_tma = true;  // the persistent bulk-copy kernel is the default
+
+size_t gemv_q8_stream_smem(int n) {
+    return size_t(kPS) * kPStage + size_t(n) + size_t(n / 64) * 4 * (1 + 2 * kPR);
+}
+
+int gemv_q8_stream(cudaStream_t st, float *y, const int8_t *xq, const float *xs,
+                   const int8_t *wq, const float *ws, int n, int d, const float *res, int *err) {
+    static bool attr[kMaxDevices] = {};
+    const size_t smem = gemv_q8_stream_smem(n);
+    const int r = set_smem_attr(reinterpret_cast<const void *>(gemv_q8_stream_kernel), attr,
+                                kGemvSmemMax, "cudaFuncSetAttribute(gemv_q8_stream)");
+    if (r != LEAP_OK) return r;
+    int dev = 0, sms = 0, per_sm = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+        &per_sm, gemv_q8_stream_kernel, kPThreads, smem);
+    if (e != cudaSuccess) return cuda_status(e, "gemv_q8_stream occupancy");
+    const int nblocks = (d + kPR - 1) / kPR;
+    const int grid = std::max(1, std::min(nblocks, sms * std::max(per_sm, 1)));
+    return launch_pdl("gemv_q8_stream", gemv_q8_stream_kernel, dim3(unsigned(grid)),
+                      dim3(kPThreads), smem, st, y, xq, xs, wq, ws, n, d, res, err);
+}
 
 int gemv_q8_slice(cudaStream_t st, float *y, const int8_t *xq, const float *xs, const int8_t *wq,
                   const float *ws, int n, int d, const float *res, size_t smem) {
@@ -768,6 +966,8 @@ int gemv_q8(cudaStream_t st, float *y, const int8_t *xq, const float *xs, const 
     // x, its scales and the per-row group dots live in shared memory; beyond
     // that the tiled kernel (same accumulation order) takes over
     if (smem > kGemvSmemMax) return gemm_q8(st, y, xq, xs, wq, ws, n, d, 1, res);
+    if (g_q8_tma && gemv_q8_stream_smem(n) <= kGemvSmemMax)
+        return gemv_q8_stream(st, y, xq, xs, wq, ws, n, d, res, err);
     if (g_q8_slice) return gemv_q8_slice(st, y, xq, xs, wq, ws, n, d, res, smem);
     static bool attr[kMaxDevices] = {};
     const int r = set_smem_attr(reinterpret_cast<const void *>(gemv_q8_kernel), attr, kGemvSmemMax,

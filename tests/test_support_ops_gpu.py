@@ -59,11 +59,11 @@ def _qmm(xq, xs, wq, ws, n, d, T, res=None):
     return y
 
 
-@pytest.fixture(params=[0, 1], ids=["sliced", "regs"])
+@pytest.fixture(params=[0, 1, 2], ids=["sliced", "regs", "stream"])
 def q8_gemv(request):
     check(lib().leap_op_set_q8_gemv(request.param))
     yield request.param
-    check(lib().leap_op_set_q8_gemv(0))
+    check(lib().leap_op_set_q8_gemv(2))  # the library default
 
 
 @pytest.mark.parametrize("n,d", [(2048, 256), (4096, 6144), (14336, 4096), (8192, 1024),
