@@ -384,6 +384,29 @@ LEAP_API int leap_op_set_q8_gemv(int impl);
  * first maximum in the reference's scan order. */
 LEAP_API int leap_op_argmax(void *stream, int *token, const float *v, int n);
 
+/* ---- sampler (src/inference/Sampler.cpp, Utils.h:18-29) ------------------
+ * The reference Sampler(vocab, temperature, topp, seed) on the GPU.  Each
+ * leap_sampler_sample is one Sampler::sample(logits): temperature 0 ->
+ * argmax; else softmax(logits / temperature) and a coin from the same
+ * xorshift* state (advanced on the host, one draw per call), then
+ * multinomial (topp <= 0 or >= 1) or top-p sampling.  Logits are device
+ * memory and are not modified; the token is written to device memory,
+ * stream-ordered.  Equal probabilities are taken in index order; a token can
+ * differ from the reference's only when a running probability sum lies
+ * within float rounding of the coin or of topp. */
+typedef struct leap_sampler leap_sampler;
+LEAP_API int leap_sampler_create(int vocab, float temperature, float topp,
+                                 unsigned long long seed, int device, leap_sampler **out);
+LEAP_API int leap_sampler_destroy(leap_sampler *s);
+LEAP_API int leap_sampler_sample(leap_sampler *s, void *stream, const float *logits,
+                                 int *token_dev);
+/* The RNG state after the draws so far (the reference's rng_state). */
+LEAP_API int leap_sampler_state(const leap_sampler *s, unsigned long long *state);
+
+/* Tokens from leap_engine_forward / _head come from this sampler instead of
+ * the greedy argmax (NULL restores argmax).  The engine does not own it. */
+LEAP_API int leap_engine_set_sampler(leap_engine *e, leap_sampler *s);
+
 /* ---- stage-to-stage transport (layer-range pipelines in one box) --------
  * Replaces the reference's ring transport between a master and its workers
  * (src/inference/FloatTransformer.cpp:772-793 and :800-946, TCP/UDP or the

@@ -13,5 +13,6 @@ __all__ = ["AttentionContext", "LeapError", "rope_table", "LIB_PATH"]
 __version__ = "0.1.0"
 from .engine import FLAG_NEED_REPLY, FLAG_NO_REPLY, Transformer  # noqa: E402
 from .modelfile import ModelConfig  # noqa: E402
+from .sampler import Sampler  # noqa: E402
 
-__all__ += ["Transformer", "ModelConfig", "FLAG_NEED_REPLY", "FLAG_NO_REPLY"]
+__all__ += ["Transformer", "ModelConfig", "FLAG_NEED_REPLY", "FLAG_NO_REPLY", "Sampler"]

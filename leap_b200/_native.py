@@ -107,6 +107,12 @@ SIGNATURES: dict[str, tuple] = {
     "leap_op_qmatmul": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                 c_int, c_int, c_int, c_int, c_void_p]),
     "leap_op_argmax": (c_int, [c_void_p, c_void_p, c_void_p, c_int]),
+    "leap_sampler_create": (c_int, [c_int, ctypes.c_float, ctypes.c_float, ctypes.c_ulonglong, c_int,
+                                    ctypes.POINTER(c_void_p)]),
+    "leap_sampler_destroy": (c_int, [c_void_p]),
+    "leap_sampler_sample": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p]),
+    "leap_sampler_state": (c_int, [c_void_p, ctypes.POINTER(ctypes.c_ulonglong)]),
+    "leap_engine_set_sampler": (c_int, [c_void_p, c_void_p]),
     "leap_pp_unique_id": (c_int, [c_void_p]),
     "leap_pp_init": (c_int, [c_void_p, c_int, c_int, c_int, c_int, ctypes.POINTER(c_void_p)]),
     "leap_pp_send_next": (c_int, [c_void_p, c_void_p, ctypes.c_size_t, c_void_p]),

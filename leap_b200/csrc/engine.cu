@@ -525,7 +525,9 @@ int head(leap_engine *e, float *x, float *logits, int *token) {
         ETRY(rmsnorm(e->stream, x, x, e->rms_final, 1, c.dim));
     float *lg = logits ? logits : e->logits;
     ETRY(linear_vec(e, lg, x, e->wcls, 0, c.vocab_size, nullptr));
-    if (token) ETRY(argmax(e->stream, token, lg, c.vocab_size));
+    if (token)
+        ETRY(e->sampler ? leap::sampler_launch(e->sampler, e->stream, lg, token)
+                        : argmax(e->stream, token, lg, c.vocab_size));
     return LEAP_OK;
 }
 
@@ -843,6 +845,16 @@ int leap_op_set_q8_gemv(int impl) {
     }
     leap::eng::g_q8_slice = impl == 0;
     leap::eng::g_q8_tma = impl == 2;
+    return LEAP_OK;
+}
+
+int leap_engine_set_sampler(leap_engine *e, leap_sampler *s) {
+    leap::clear_error();
+    if (!e) {
+        leap::set_error("null engine");
+        return LEAP_ERR_INVALID;
+    }
+    e->sampler = s;
     return LEAP_OK;
 }
 

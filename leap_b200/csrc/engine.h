@@ -32,6 +32,10 @@ int silu_mul(cudaStream_t st, float *h, const float *h3, size_t n);
 int silu_mul_quantize(cudaStream_t st, int8_t *q, float *s, const float *h, const float *h3,
                       size_t n);
 int argmax(cudaStream_t st, int *out, const float *v, int n);
+}  // namespace eng
+// One Sampler::sample on device logits (sampler.cu).
+int sampler_launch(leap_sampler *s, cudaStream_t st, const float *logits, int *token_dev);
+namespace eng {
 int synth_normal(cudaStream_t st, float *w, size_t n, uint64_t seed, float std, float fill);
 
 // A weight matrix [rows][cols]: FP32, or int8 with one float scale per group
@@ -69,6 +73,7 @@ struct leap_engine {
     int8_t *aq = nullptr;
     float *as = nullptr;
     int *tok_dev = nullptr, *argmax_dev = nullptr;
+    leap_sampler *sampler = nullptr;  // not owned; NULL = greedy argmax
     int *h_tok = nullptr;  // pinned host mirror for token ids
 
     // prompt-chunk activations, max_chunk tokens

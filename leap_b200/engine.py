@@ -108,8 +108,16 @@ class Transformer:
         self.last_token = nxt.value
         return self._logits.copy()
 
+    def set_sampler(self, sampler) -> None:
+        """Next tokens from `sampler` (a leap_b200.Sampler on this engine's
+        device) instead of the greedy argmax; None restores argmax.  The
+        engine keeps a reference, not ownership."""
+        self._sampler = sampler
+        check(lib().leap_engine_set_sampler(self.handle,
+                                            sampler.handle if sampler is not None else None))
+
     def forward_argmax(self, token: int, pos: int) -> int:
-        """Greedy next token (Sampler at temperature 0)."""
+        """Next token: the greedy argmax, or the draw of the sampler set."""
         nxt = ctypes.c_int()
         check(lib().leap_engine_forward(self.handle, token, pos, None, ctypes.byref(nxt)))
         return nxt.value

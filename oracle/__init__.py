@@ -269,6 +269,31 @@ def ref_argmax(v) -> int:
     return int(lib.leapref_sample_argmax(_p(a), int(a.size)))
 
 
+def ref_sample(logits, temperature: float, topp: float, state: int) -> int:
+    """One draw of the reference Sampler (src/inference/Sampler.cpp:187-232)
+    with its RNG state starting at `state` (advance it with random_f32)."""
+    a = np.ascontiguousarray(logits, np.float32)
+    lib = _load(REF_ENGINE_SO)
+    lib.leapref_sample.argtypes = [_f, _int, ctypes.c_float, ctypes.c_float, ctypes.c_ulonglong]
+    return int(lib.leapref_sample(_p(a), int(a.size), float(temperature), float(topp), int(state)))
+
+
+def random_u32(state: int):
+    """The reference's xorshift* step (src/inference/Utils.h:18-24):
+    returns (value, new state)."""
+    m = (1 << 64) - 1
+    state ^= state >> 12
+    state = (state ^ (state << 25)) & m
+    state ^= state >> 27
+    return ((state * 0x2545F4914F6CDD1D) & m) >> 32, state
+
+
+def random_f32(state: int):
+    """A float in [0, 1) (src/inference/Utils.h:26-29): (value, new state)."""
+    u, state = random_u32(state)
+    return float(np.float32(u >> 8) / np.float32(16777216.0)), state
+
+
 def has_ref_engine() -> bool:
     return os.path.exists(REF_ENGINE_SO) and os.path.exists(REF_ENGINE_10K_SO)
 

@@ -76,4 +76,16 @@ int leapref_sample_argmax(const float *logits, int vocab) {
     return s.sample(tmp.get());
 }
 
+// One draw of the reference Sampler (src/inference/Sampler.cpp:187-232) with
+// the given temperature and top-p, its RNG state starting at *state.  The
+// Sampler keeps its state private, so the caller advances *state itself
+// (one random_f32 per draw when temperature != 0, src/inference/Utils.h:18-29).
+int leapref_sample(const float *logits, int vocab, float temperature, float topp,
+                   unsigned long long state) {
+    Inference::Sampler s(vocab, temperature, topp, state);
+    std::unique_ptr<float[]> tmp(new float[vocab]);
+    std::memcpy(tmp.get(), logits, sizeof(float) * vocab);
+    return s.sample(tmp.get());
+}
+
 }  // extern "C"

@@ -1,0 +1,141 @@
+"""The GPU sampler against the reference Sampler (src/inference/Sampler.cpp)
+on the same logits and the same generator states.
+
+The GPU walks the reference's running sums in the reference's float order,
+but its probabilities differ from the reference's in the last bits (exp,
+softmax summation order).  A token can therefore differ where the coin, or
+topp, lies within that rounding of a running sum — and since every token
+has such a boundary, the chance per draw grows with the number of tokens in
+the walk (about n x 1e-7: below 1 % for top-p sets of thousands, a few
+percent for a multinomial walk over 128k tokens).  So each mismatch must sit
+at the same place of the reference's walk, within 1e-4 of running mass, and
+at least 95 % of the draws must be identical."""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from leap_b200 import Sampler
+from leap_b200._native import check, lib
+
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(not oracle.has_ref_engine(), reason="oracle/_ref not built")]
+
+
+def _logits(rng, n, scale):
+    return (rng.standard_normal(n) * scale).astype(np.float32)
+
+
+def _walk_position(lg, temperature, topp, token):
+    """Running mass before `token` in the reference's walk order: index
+    order for multinomial, descending probability for top-p."""
+    x = lg.astype(np.float64) / temperature
+    p = np.exp(x - x.max())
+    p /= p.sum()
+    if 0 < topp < 1:
+        order = np.argsort(-p, kind="stable")
+    else:
+        order = np.arange(p.size)
+    where = np.empty(p.size, np.int64)
+    where[order] = np.arange(p.size)
+    cum = np.concatenate([[0.0], np.cumsum(p[order])])
+    return cum[where[token]]
+
+
+@pytest.mark.parametrize("vocab", [32000, 128256])
+@pytest.mark.parametrize("temperature,topp", [(1.0, 0.9), (0.7, 0.5), (1.2, 0.9),
+                                              (1.0, 0.0), (0.8, 1.0)])
+def test_sampler_matches_reference(cuda, vocab, temperature, topp):
+    rng = np.random.default_rng(vocab + int(temperature * 100) + int(topp * 1000))
+    seed = int(rng.integers(1, 1 << 62))
+    draws, agree, mismatches = 60, 0, []
+    with Sampler(vocab, temperature, topp, seed) as s:
+        state = seed
+        for i in range(draws):
+            lg = _logits(rng, vocab, 4.0 + 2 * (i % 3))
+            got = s.sample(torch.from_numpy(lg).cuda())
+            ref = oracle.ref_sample(lg, temperature, topp, state)
+            _, state = oracle.random_f32(state)
+            if got == ref:
+                agree += 1
+            else:
+                gap = abs(_walk_position(lg, temperature, topp, got)
+                          - _walk_position(lg, temperature, topp, ref))
+                mismatches.append((i, got, ref, gap))
+                assert gap <= 1e-4, mismatches
+        assert s.state == state  # one generator step per draw, as the reference
+    assert agree >= 0.95 * draws, mismatches
+
+
+def test_flat_distribution_beyond_the_sort(cuda):
+    """Logits of std 2 at temperature 1.3, top-p 0.95 over 128256 tokens put
+    tens of thousands of candidates in play; beyond the 16384 sorted in
+    shared memory the walks use exact sums where the reference's float sums
+    drift, so a few percent of tokens may differ.  They must stay in the
+    reference's top-p set and agree mostly."""
+    vocab, temperature, topp = 128256, 1.3, 0.95
+    rng = np.random.default_rng(99)
+    state = seed = 2024
+    agree = 0
+    with Sampler(vocab, temperature, topp, seed) as s:
+        for i in range(20):
+            lg = _logits(rng, vocab, 2.0)
+            got = s.sample(torch.from_numpy(lg).cuda())
+            ref = oracle.ref_sample(lg, temperature, topp, state)
+            _, state = oracle.random_f32(state)
+            agree += got == ref
+            x = lg * np.float32(1 / temperature)
+            p = np.exp(x - x.max())
+            p /= p.sum()
+            order = np.argsort(-p, kind="stable")
+            top = order[:int(np.searchsorted(np.cumsum(p[order]), topp)) + 2]
+            assert got in set(top.tolist())
+    assert agree >= 16
+
+
+def test_temperature_zero_is_argmax(cuda):
+    rng = np.random.default_rng(5)
+    lg = _logits(rng, 128256, 3.0)
+    d = torch.from_numpy(lg).cuda()
+    with Sampler(128256, 0.0, 0.9, 17) as s:
+        assert s.sample(d) == oracle.ref_argmax(lg)
+        assert s.state == 17  # greedy draws do not touch the generator
+
+
+def test_peaked_distribution_and_ties(cuda):
+    """One token holding nearly all the mass is always drawn; with two equal
+    top tokens the draw stays between them."""
+    n = 50000
+    lg = np.full(n, -20.0, np.float32)
+    lg[777] = 5.0
+    d = torch.from_numpy(lg).cuda()
+    with Sampler(n, 1.0, 0.9, 3) as s:
+        assert all(s.sample(d) == 777 for _ in range(20))
+    lg[12345] = 5.0
+    d = torch.from_numpy(lg).cuda()
+    with Sampler(n, 1.0, 0.9, 4) as s:
+        seen = {s.sample(d) for _ in range(40)}
+    assert seen <= {777, 12345} and len(seen) == 2
+
+
+def test_engine_uses_the_sampler(cuda, tmp_path):
+    """A single-stage engine with a sampler set returns the sampler's draw on
+    the logits it returns; with the sampler removed it is greedy again."""
+    from leap_b200 import ModelConfig, Transformer
+    cfg = ModelConfig(dim=512, hidden_dim=1024, n_layers=2, n_heads=8, n_kv_heads=2,
+                      vocab_size=1000, seq_len=64)
+    eng = Transformer.synthetic(cfg, False, seed=3, device=0, rope_theta=10000.0)
+    try:
+        logits = eng.forward(5, 0)
+        assert eng.last_token == int(np.argmax(logits))
+        eng.clear_kv_cache()
+        with Sampler(1000, 1.0, 0.9, 11) as s, Sampler(1000, 1.0, 0.9, 11) as twin:
+            eng.set_sampler(s)
+            logits = eng.forward(5, 0)
+            expect = twin.sample(torch.from_numpy(logits).cuda())
+            assert eng.last_token == expect
+            eng.set_sampler(None)
+    finally:
+        eng.close()
