@@ -12,9 +12,10 @@
 //   warps 4-11 (256 threads): convert the FP32 K/V tile j+2 staged by bulk
 //              copies into TF32 hi/lo operand tiles (K-major, 128-byte
 //              swizzle; V transposed);
-//   warp 12    (one elected lane): issue the bulk copies and every tcgen05.mma:
-//              S(j+1) = Q K(j+1)^T is computed while the softmax works on
-//              S(j), then O += P(j) V(j).
+//   warp 12    (one elected lane): issue the bulk copies and every tcgen05.mma,
+//              whichever is ready first (S(j+1) = Q K(j+1)^T runs while the
+//              softmax works on S(j); O += P(j) V(j) as soon as P(j) is in
+//              TMEM; a stage's next copy as soon as the converters free it).
 //
 // Key tiles are 32 keys so that everything can be double-buffered:
 //   TMEM (512 columns): Q hi [0,128) Q lo [128,256) O [256,384)
