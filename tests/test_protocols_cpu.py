@@ -1,0 +1,203 @@
+"""The mbarrier hand-off protocols of two warp-specialised kernels, modelled
+on the CPU and run under random interleavings (no GPU).
+
+Each model follows its kernel step for step: waits on a barrier phase (the
+parity of item j's use of a buffer is (j / buffers) & 1), arrivals, the
+tensor core or copy engine completing asynchronously.  Every run must
+finish (no deadlock), no wait may target a phase more than one behind the
+barrier (parities would alias), and every buffer is read only after it was
+written for that item and rewritten only after its readers are done.
+
+  prefill_tc_pipe.cu  softmax warps / converter warps / one issuing lane;
+                      the issuer takes whichever of S(j), PV(j), copy(j) is
+                      ready; MMAs complete in issue order.
+  engine_kernels.cu   gemv_q8_stream_kernel: dot warps / copy producer /
+                      chain warp over (row block, chunk) items.
+"""
+import random
+
+import pytest
+
+
+class Bar:
+    def __init__(self, count):
+        self.count, self.pending, self.done = count, count, 0
+
+    def arrive(self):
+        self.pending -= 1
+        if self.pending == 0:
+            self.done += 1
+            self.pending = self.count
+
+    def ready(self, use):
+        """Has the phase of this barrier's use number `use` completed?"""
+        assert self.done <= use + 1, ("parity would alias", self.done, use)
+        return self.done >= use + 1
+
+
+def run_prefill(n_kt, seed, rescale_prob, n_conv=8):
+    R = random.Random(seed)
+    B = {}
+    for b in (0, 1):
+        for k, c in (("stf", 1), ("ste", n_conv), ("opf", n_conv), ("ope", 1), ("sf", 1),
+                     ("pf", 4)):
+            B[(k, b)] = Bar(c)
+    st = {"stage": {}, "op": {}, "S": {}, "P": {}, "O": 0}
+    mma, cps = [], []
+    sm = [{"j": 0, "ph": 0} for _ in range(4)]
+    cv = [{"j": 0} for _ in range(n_conv)]
+    iss = {"ns": 0, "np": 0, "staged": 0}
+    for j in range(min(2, n_kt)):
+        cps.append(j)
+        iss["staged"] += 1
+    for _ in range(200000):
+        acts = []
+        for w, s in enumerate(sm):
+            j = s["j"]
+            if j >= n_kt:
+                if s["ph"] == 0 and B[("ope", (n_kt - 1) & 1)].ready((n_kt - 1) >> 1):
+                    acts.append(("smfin", w))
+                continue
+            b = j & 1
+            if s["ph"] == 0 and B[("sf", b)].ready(j >> 1):
+                acts.append(("smS", w, False))
+            elif s["ph"] == 1:
+                resc = j > 0 and R.random() < rescale_prob
+                if not resc or B[("ope", b ^ 1)].ready((j - 1) >> 1):
+                    acts.append(("smP", w, resc))
+        for w, s in enumerate(cv):
+            j = s["j"]
+            if j < n_kt and B[("stf", j & 1)].ready(j >> 1) and \
+                    (j < 2 or B[("ope", j & 1)].ready((j - 2) >> 1)):
+                acts.append(("cv", w))
+        ns, np_, sg = iss["ns"], iss["np"], iss["staged"]
+        if ns < n_kt and ns <= np_ + 1 and B[("opf", ns & 1)].ready(ns >> 1) and \
+                (ns < 2 or B[("ope", ns & 1)].ready((ns - 2) >> 1)):
+            acts.append(("S",))
+        if np_ < ns and B[("pf", np_ & 1)].ready(np_ >> 1):
+            acts.append(("PV",))
+        if sg < n_kt and B[("ste", sg & 1)].ready((sg - 2) >> 1):
+            acts.append(("stage",))
+        if mma:
+            acts.append(("mma",))
+        acts += [("cp",)] * len(cps)
+        if not acts:
+            finished = np_ >= n_kt and all(s["ph"] == 2 for s in sm) and not mma and not cps
+            return "ok" if finished else "deadlock"
+        a = R.choice(acts)
+        if a[0] == "smS":
+            w = a[1]
+            j = sm[w]["j"]
+            assert st["S"].get((j & 1, w)) == ("S", j)
+            sm[w]["ph"] = 1
+        elif a[0] == "smP":
+            w, j = a[1], sm[a[1]]["j"]
+            if a[2]:
+                assert st["O"] == j  # O holds PV(0..j-1) when it is rescaled
+            st["P"][(j & 1, w)] = j
+            st["S"][(j & 1, w)] = ("P", j)
+            B[("pf", j & 1)].arrive()
+            sm[w]["j"] += 1
+            sm[w]["ph"] = 0
+        elif a[0] == "smfin":
+            assert st["O"] == n_kt
+            sm[a[1]]["ph"] = 2
+        elif a[0] == "cv":
+            w, j = a[1], cv[a[1]]["j"]
+            assert st["stage"].get(j & 1) == j
+            st["op"][(j & 1, w)] = j
+            B[("ste", j & 1)].arrive()
+            B[("opf", j & 1)].arrive()
+            cv[w]["j"] += 1
+        elif a[0] == "S":
+            j = iss["ns"]
+            assert all(st["op"].get((j & 1, w)) == j for w in range(n_conv))
+            assert all(st["P"].get((j & 1, w)) in (None, j - 2) for w in range(4))
+            mma.append(("S", j))
+            iss["ns"] += 1
+        elif a[0] == "PV":
+            j = iss["np"]
+            assert all(st["P"].get((j & 1, w)) == j for w in range(4))
+            assert all(st["op"].get((j & 1, w)) == j for w in range(n_conv))
+            mma.append(("PV", j))
+            iss["np"] += 1
+        elif a[0] == "stage":
+            cps.append(iss["staged"])
+            iss["staged"] += 1
+        elif a[0] == "mma":  # the tensor core completes in issue order
+            kind, j = mma.pop(0)
+            if kind == "S":
+                for w in range(4):
+                    st["S"][(j & 1, w)] = ("S", j)
+                B[("sf", j & 1)].arrive()
+            else:
+                assert st["O"] == j
+                st["O"] = j + 1
+                B[("ope", j & 1)].arrive()
+        else:  # a copy lands (copies complete in any order)
+            j = cps.pop(R.randrange(len(cps)))
+            st["stage"][j & 1] = j
+            B[("stf", j & 1)].arrive()
+    return "livelock"
+
+
+def run_gemv(items, seed, n_stages=3, n_dot=8):
+    R = random.Random(seed)
+    full = [Bar(1) for _ in range(n_stages)]
+    empty = [Bar(n_dot) for _ in range(n_stages)]
+    ready = [Bar(n_dot), Bar(n_dot)]
+    done = [Bar(1), Bar(1)]
+    stage, tab = {}, {}
+    dots = [0] * n_dot
+    chain = 0
+    issued = min(n_stages, items)
+    cps = list(range(issued))
+    for _ in range(200000):
+        acts = []
+        for w in range(n_dot):
+            it = dots[w]
+            if it < items and full[it % n_stages].ready(it // n_stages) and \
+                    (it < 2 or done[it & 1].ready((it - 2) >> 1)):
+                acts.append(("dot", w))
+        if issued < items and empty[issued % n_stages].ready((issued - n_stages) // n_stages):
+            acts.append(("issue",))
+        if chain < items and ready[chain & 1].ready(chain >> 1):
+            acts.append(("chain",))
+        acts += [("cp",)] * len(cps)
+        if not acts:
+            return "ok" if chain == items and all(d == items for d in dots) else "deadlock"
+        a = R.choice(acts)
+        if a[0] == "dot":
+            w, it = a[1], dots[a[1]]
+            assert stage.get(it % n_stages) == it  # the stage holds this item
+            assert tab.get((it & 1, w)) in (None, it - 2)  # the chain consumed the last use
+            tab[(it & 1, w)] = it
+            empty[it % n_stages].arrive()
+            ready[it & 1].arrive()
+            dots[w] += 1
+        elif a[0] == "issue":
+            assert all(d > issued - n_stages for d in dots)  # nobody still reads the stage
+            cps.append(issued)
+            issued += 1
+        elif a[0] == "chain":
+            assert all(tab.get((chain & 1, w)) == chain for w in range(n_dot))
+            done[chain & 1].arrive()
+            chain += 1
+        else:
+            it = cps.pop(R.randrange(len(cps)))
+            stage[it % n_stages] = it
+            full[it % n_stages].arrive()
+    return "livelock"
+
+
+@pytest.mark.parametrize("n_kt", [1, 2, 3, 4, 7, 10])
+def test_prefill_pipeline_protocol(n_kt):
+    for seed in range(150):
+        for rp in (0.0, 0.5, 1.0):
+            assert run_prefill(n_kt, seed, rp) == "ok", (n_kt, seed, rp)
+
+
+@pytest.mark.parametrize("items", [1, 2, 3, 4, 5, 9, 16])
+def test_gemv_stream_protocol(items):
+    for seed in range(300):
+        assert run_gemv(items, seed) == "ok", (items, seed)
