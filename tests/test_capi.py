@@ -81,3 +81,39 @@ def test_no_gpu_fails_loudly():
     from leap_b200 import AttentionContext, LeapError
     with pytest.raises(LeapError):
         AttentionContext(1, 8, 8, 64, 32, bind_torch_stream=False)
+
+
+def test_header_compiles_and_links_as_c_and_cpp(tmp_path):
+    """An engine's view of the boundary: include/leap_b200.h compiles as C11
+    and C++20 and a program calling the entry points links against the
+    library (nothing is run)."""
+    import shutil
+    import subprocess
+    prog = r"""
+#include "leap_b200.h"
+#include <stddef.h>
+int use_all(void) {
+    leap_ctx *c = NULL; leap_engine *e = NULL; leap_sampler *s = NULL; leap_pp *pp = NULL;
+    float q[1] = {0.f}, o[1] = {0.f}; int tok = 0; unsigned long long st = 0;
+    int r = leap_attn_decode_host(c, 0, 0, q, q, q, o);
+    r |= leap_engine_forward(e, 1, 0, o, &tok);
+    r |= leap_sampler_create(32000, 0.8f, 0.9f, 1234ULL, 0, &s);
+    r |= leap_sampler_state(s, &st);
+    r |= leap_engine_set_sampler(e, s);
+    r |= leap_pp_send_next(pp, q, sizeof q, NULL);
+    return r;
+}
+int main(void) { return use_all() == 12345; }
+"""
+    lib = os.path.join(ROOT, "leap_b200", "lib")
+    inc = os.path.join(ROOT, "include")
+    for cc, std, ext in (("gcc", "-std=c11", "c"), ("g++", "-std=c++20", "cpp")):
+        if not shutil.which(cc):
+            pytest.skip(f"{cc} not available")
+        src = tmp_path / f"use.{ext}"
+        src.write_text(prog)
+        out = tmp_path / f"use_{ext}"
+        r = subprocess.run([cc, std, "-Wall", "-Werror", f"-I{inc}", str(src), "-o", str(out),
+                            f"-L{lib}", "-lleap_b200", f"-Wl,-rpath,{lib}"],
+                           capture_output=True, text=True)
+        assert r.returncode == 0, r.stderr
