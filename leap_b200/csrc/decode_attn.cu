@@ -91,7 +91,7 @@ decode_attn_kernel(const DecodeArgs a, const DecodeSeq tab) {
     __shared__ uint64_t full_bar[kStages];
     __shared__ float red_m[C::NGRP][G], red_l[C::NGRP][G];
     __shared__ float s_M[G], s_L[G];
-    __shared__ uint64_t comb_bar;
+    __shared__ uint64_t comb_bar, comb_bar_o;  // (M, L) table; partial outputs
     __shared__ int s_last;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -123,6 +123,7 @@ decode_attn_kernel(const DecodeArgs a, const DecodeSeq tab) {
     if (tid == 0) {
         for (int s = 0; s < kStages; ++s) mbar_init(&full_bar[s], 1);
         mbar_init(&comb_bar, 1);
+        mbar_init(&comb_bar_o, 1);
         fence_mbar_init();
     }
     __syncthreads();
@@ -380,22 +381,25 @@ decode_attn_kernel(const DecodeArgs a, const DecodeSeq tab) {
     float *sO = cW + ((nsplit * G + 3) & ~3);            // [cap][G*HD]
     const int cap = int((C::kSmem / sizeof(float) - size_t(sO - sK)) / (G * HD));
     const int n0 = min(cap, nsplit);
+    // The (M, L) table and the partials arrive on separate barriers, so the
+    // weights are formed while the partials are still on their way.
     uint32_t cphase = 0;
     if (tid == 0) {
         fence_proxy_async_global();
         const uint32_t ml_bytes = uint32_t(nsplit) * C::MLS * 4;
         const uint32_t o_bytes = uint32_t(n0) * G * HD * 4;
-        mbar_arrive_expect_tx(&comb_bar, ml_bytes + o_bytes);
+        mbar_arrive_expect_tx(&comb_bar, ml_bytes);
         bulk_g2s(sML, a.part_ml + size_t(pfirst) * C::MLS, ml_bytes, &comb_bar);
-        bulk_g2s(sO, a.part_o + size_t(pfirst) * G * HD, o_bytes, &comb_bar);
+        mbar_arrive_expect_tx(&comb_bar_o, o_bytes);
+        bulk_g2s(sO, a.part_o + size_t(pfirst) * G * HD, o_bytes, &comb_bar_o);
     }
-    bool cok = mbar_wait(&comb_bar, cphase);
+    bool cok = mbar_wait(&comb_bar, 0);
     cok = __syncthreads_and(cok);
     if (!cok) {
+        (void)mbar_wait(&comb_bar_o, 0);  // let the partials' copy land first
         if (tid == 0) report_error(a.err, kDevWaitTimeout);
         return;
     }
-    cphase ^= 1u;
     // one warp per head: max, rescaled sum, normalised weights
     for (int g = warp; g < G; g += C::WARPS) {
         float M = -INFINITY;
@@ -411,7 +415,13 @@ decode_attn_kernel(const DecodeArgs a, const DecodeSeq tab) {
         for (int sp = lane; sp < nsplit; sp += 32)
             cW[sp * G + g] = fast_exp2(sML[sp * C::MLS + 2 * g] - M) * inv;
     }
-    __syncthreads();
+    cok = mbar_wait(&comb_bar_o, cphase);  // the first chunk of partials
+    cok = __syncthreads_and(cok);  // also: every weight is in cW
+    if (!cok) {
+        if (tid == 0) report_error(a.err, kDevWaitTimeout);
+        return;
+    }
+    cphase ^= 1u;
     constexpr int kPerThread = (C::NV4 + C::THREADS - 1) / C::THREADS;
     float4 acc[kPerThread];
 #pragma unroll
@@ -422,10 +432,10 @@ decode_attn_kernel(const DecodeArgs a, const DecodeSeq tab) {
             __syncthreads();  // every thread is done with the previous chunk
             if (tid == 0) {
                 const uint32_t o_bytes = uint32_t(n) * G * HD * 4;
-                mbar_arrive_expect_tx(&comb_bar, o_bytes);
-                bulk_g2s(sO, a.part_o + size_t(pfirst + s0) * G * HD, o_bytes, &comb_bar);
+                mbar_arrive_expect_tx(&comb_bar_o, o_bytes);
+                bulk_g2s(sO, a.part_o + size_t(pfirst + s0) * G * HD, o_bytes, &comb_bar_o);
             }
-            cok = mbar_wait(&comb_bar, cphase);
+            cok = mbar_wait(&comb_bar_o, cphase);
             cok = __syncthreads_and(cok);
             if (!cok) {
                 if (tid == 0) report_error(a.err, kDevWaitTimeout);
