@@ -5,7 +5,10 @@ Every ``leap_b200/csrc/*.cu`` is compiled by nvcc for ``sm_100a`` only
 into one shared library with the CUDA runtime linked statically.  The
 library is built in-tree so that it travels with the repository snapshot.
 
-Run ``python -m leap_b200.build`` (or ``__graft_entry__.build()``).
+Run ``python -m leap_b200.build`` (or ``__graft_entry__.build()``).  With
+``--clean`` every object and the library are rebuilt from source, so a source
+that no longer compiles cannot hide behind an object left from an earlier
+build.  ``__graft_entry__.build()`` always builds clean.
 """
 from __future__ import annotations
 
@@ -63,8 +66,19 @@ def _compile(src: str, extra: list[str]) -> str:
     return obj
 
 
-def build(verbose: bool = False, extra: list[str] | None = None) -> str:
-    """Compile every CUDA source for sm_100a and link the shared library."""
+def clean() -> None:
+    """Remove the object directory and the linked library."""
+    shutil.rmtree(OBJ, ignore_errors=True)
+    if os.path.exists(LIB):
+        os.remove(LIB)
+
+
+def build(verbose: bool = False, extra: list[str] | None = None, fresh: bool = False) -> str:
+    """Compile every CUDA source for sm_100a and link the shared library.
+
+    ``fresh`` discards earlier objects first (see :func:`clean`)."""
+    if fresh:
+        clean()
     os.makedirs(OBJ, exist_ok=True)
     os.makedirs(LIBDIR, exist_ok=True)
     srcs = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
@@ -82,4 +96,6 @@ def build(verbose: bool = False, extra: list[str] | None = None) -> str:
 
 
 if __name__ == "__main__":
-    build(verbose=True, extra=sys.argv[1:])
+    args = sys.argv[1:]
+    fresh = "--clean" in args
+    build(verbose=True, extra=[a for a in args if a != "--clean"], fresh=fresh)

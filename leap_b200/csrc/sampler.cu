@@ -28,6 +28,7 @@
 // the coin or topp lies within that rounding of a running sum.
 #include <cmath>
 #include <cstdint>
+#include <mutex>
 
 #include "common.cuh"
 #include "ctx.h"
@@ -370,13 +371,23 @@ int sampler_launch(leap_sampler *s, cudaStream_t st, const float *logits, int *t
     const unsigned u = unsigned((x * 0x2545F4914F6CDD1Dull) >> 32);
     const unsigned coin24 = u >> 8;  // coin = coin24 / 2^24 exactly
     const float inv_temp = 1.0f / s->temperature;
-    static bool attr[kMaxDevices] = {};
-    if (s->device < kMaxDevices && !attr[s->device]) {
-        const cudaError_t e = cudaFuncSetAttribute(sample_kernel,
-                                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                   int(kSortCap * sizeof(uint64_t)));
-        if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(sample_kernel)");
-        attr[s->device] = true;
+    if (s->device < 0 || s->device >= kMaxDevices) {
+        set_error("sampler: device index out of range");
+        return LEAP_ERR_INVALID;
+    }
+    {
+        // The dynamic shared-memory opt-in is a per-device function attribute: set it once
+        // per device, under a lock so that samplers on several host threads do not race.
+        static std::mutex smem_attr_mu;
+        static bool smem_attr_set[kMaxDevices] = {};
+        std::lock_guard<std::mutex> lk(smem_attr_mu);
+        if (!smem_attr_set[s->device]) {
+            const cudaError_t e = cudaFuncSetAttribute(sample_kernel,
+                                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                       int(kSortCap * sizeof(uint64_t)));
+            if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(sample_kernel)");
+            smem_attr_set[s->device] = true;
+        }
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(1);

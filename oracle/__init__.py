@@ -50,10 +50,27 @@ def build_port() -> str:
     return PORT_SO
 
 
+def reference_root() -> str | None:
+    """Where the reference sources are: ``$LEAP_REFERENCE`` if set, else the
+    ``reference_path`` recorded in the repository's ``BASELINE.json``.  None
+    when neither names a directory holding ``src/inference``."""
+    ref = os.environ.get("LEAP_REFERENCE")
+    if not ref:
+        try:
+            import json
+            with open(os.path.join(os.path.dirname(HERE), "BASELINE.json")) as fh:
+                ref = json.load(fh).get("reference_path")
+        except (OSError, ValueError):
+            ref = None
+    if ref and os.path.isdir(os.path.join(ref, "src", "inference")):
+        return ref
+    return None
+
+
 def build_ref() -> bool:
     """Compile the reference's own code (needs the reference sources)."""
-    ref = os.environ.get("LEAP_REFERENCE", "/root/reference")
-    if not os.path.isdir(os.path.join(ref, "src", "inference")):
+    ref = reference_root()
+    if ref is None:
         return False
     subprocess.run(["make", "-s", "-C", HERE, "ref", f"REF={ref}"], check=True)
     return True
