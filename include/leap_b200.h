@@ -217,9 +217,9 @@ LEAP_API int leap_attn_prefill(leap_ctx *ctx, int slot, int layer, int pos0, int
  * reference: LEAP's CPU engine owns all its memory in std::vectors.)
  *
  * For callers that cannot call cudaMalloc: a host whose device memory is all
- * owned by one allocator or a fixed arena, code being recorded into a stream
- * or graph that must not change the device's allocations, or an embedding
- * that is not allowed to touch CUDA's allocator.  Such a caller cannot create
+ * owned by one allocator (a framework's caching allocator) or by a fixed arena
+ * reserved at start-up, or an embedding that is not allowed to touch CUDA's
+ * allocator.  Such a caller cannot create
  * a leap_ctx (which allocates the cache and scratch), so this entry point
  * takes everything as caller-owned device memory and keeps its own scratch
  * (split-KV partials, combine tickets, an error word) in a 4 MiB array
@@ -242,6 +242,11 @@ LEAP_API int leap_attn_prefill(leap_ctx *ctx, int slot, int layer, int pos0, int
  * threads) race on it and must not be issued.  A context too long for the
  * scratch (more split-KV partials than fit in 4 MiB, about 64k positions
  * for 8 kv heads of 4x128) is rejected with LEAP_ERR_INVALID and a message.
+ *
+ * The kernel's copy waits are bounded (about two seconds, never reached on a
+ * healthy GPU).  A wait that gives up leaves `out` unwritten for the heads
+ * it served and cannot be reported through this entry point; callers that
+ * need that report use leap_attn_decode.
  */
 LEAP_API int leap_attn_decode_noalloc(void *stream, int n_heads, int n_kv_heads,
                                       int head_dim, int pos,

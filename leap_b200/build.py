@@ -54,9 +54,9 @@ def _stale(target: str, deps: list[str]) -> bool:
     return any(os.path.getmtime(d) > t for d in deps)
 
 
-def _compile(src: str, extra: list[str]) -> str:
-    obj = os.path.join(OBJ, os.path.basename(src)[:-3] + ".o")
-    if _stale(obj, [src] + _headers()):
+def _compile(src: str, extra: list[str], objdir: str = OBJ, force: bool = False) -> str:
+    obj = os.path.join(objdir, os.path.basename(src)[:-3] + ".o")
+    if force or _stale(obj, [src] + _headers()):
         cmd = [nvcc(), *NVCC_FLAGS, *extra, "-c", src, "-o", obj]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
@@ -73,6 +73,29 @@ def clean() -> None:
         os.remove(LIB)
 
 
+def sources() -> list[str]:
+    return sorted(glob.glob(os.path.join(CSRC, "*.cu")))
+
+
+def _link(objs: list[str], lib: str) -> None:
+    cmd = [nvcc(), *ARCH, "-shared", "-o", lib, *objs, "-cudart", "static"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+
+
+def build_into(objdir: str, lib: str, extra: list[str] | None = None) -> str:
+    """Compile every source from scratch into ``objdir`` and link ``lib``.
+
+    Reuses nothing, so it shows whether the current sources build."""
+    os.makedirs(objdir, exist_ok=True)
+    extra = list(extra or [])
+    with cf.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 4)) as ex:
+        objs = list(ex.map(lambda s: _compile(s, extra, objdir, True), sources()))
+    _link(objs, lib)
+    return lib
+
+
 def build(verbose: bool = False, extra: list[str] | None = None, fresh: bool = False) -> str:
     """Compile every CUDA source for sm_100a and link the shared library.
 
@@ -81,15 +104,11 @@ def build(verbose: bool = False, extra: list[str] | None = None, fresh: bool = F
         clean()
     os.makedirs(OBJ, exist_ok=True)
     os.makedirs(LIBDIR, exist_ok=True)
-    srcs = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
     extra = list(extra or [])
     with cf.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 4)) as ex:
-        objs = list(ex.map(lambda s: _compile(s, extra), srcs))
+        objs = list(ex.map(lambda s: _compile(s, extra), sources()))
     if _stale(LIB, objs):
-        cmd = [nvcc(), *ARCH, "-shared", "-o", LIB, *objs, "-cudart", "static"]
-        r = subprocess.run(cmd, capture_output=True, text=True)
-        if r.returncode != 0:
-            raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+        _link(objs, LIB)
     if verbose:
         print(LIB)
     return LIB

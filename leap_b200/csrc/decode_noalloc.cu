@@ -1,15 +1,21 @@
 // decode_noalloc.cu — decode attention for callers that cannot allocate.
 //
 // Some callers cannot call cudaMalloc at all: code running under an
-// allocator that owns every device byte (a framework's caching allocator or
-// an arena handed out once at start-up), code that is being recorded into a
-// stream or graph that must not change the device's allocations, or an
-// embedding where the host side is not allowed to touch CUDA's allocator.
-// leap_attn_decode_noalloc serves them: the caller passes its own K/V cache,
-// RoPE table, inputs and output, and the only memory beyond those — the
-// split-KV partials, the combine tickets and the error word — lives in the
-// file-scope array below, which every GPU that loads this library holds
-// until the process exits.  Nothing here calls cudaMalloc or cudaFree.
+// allocator that owns every device byte (a framework's caching allocator, or
+// a serving process that reserves all device memory as one arena at
+// start-up and hands out slices of it), or an embedding whose host side is
+// not allowed to touch CUDA's allocator.  leap_attn_decode_noalloc serves
+// them: the caller passes its own K/V cache, RoPE table, inputs and output,
+// and the only memory beyond those — the split-KV partials, the combine
+// tickets and the kernel's error word — lives in the file-scope array below,
+// which every GPU that loads this library holds until the process exits.
+// Nothing here calls cudaMalloc or cudaFree.
+//
+// The kernel's copy waits are bounded (they give up after about two seconds,
+// which a healthy GPU never reaches).  A wait that gives up is recorded in the
+// array's error word, which no call reads back and the next call clears:
+// this entry point cannot report it.  Callers that need that report use the
+// context entry point leap_attn_decode, whose synchronising calls return it.
 #include <mutex>
 
 #include "common.cuh"
@@ -62,7 +68,13 @@ extern "C" int leap_attn_decode_noalloc(void *stream, int n_heads, int n_kv_head
         set_error("noalloc decode: unsupported head_dim %d / kv_mul %d", head_dim, group);
         return LEAP_ERR_INVALID;
     }
-    if (pos < 0 || head_stride < (long long)(pos + 1) * head_dim || head_stride % 4 != 0) {
+    // Far beyond what the scratch holds (about 64k positions); refused here so
+    // that no int below can overflow.
+    if (pos >= (1 << 24)) {
+        set_error("noalloc decode: pos %d is beyond what the fixed scratch can hold", pos);
+        return LEAP_ERR_INVALID;
+    }
+    if (pos < 0 || head_stride < ((long long)pos + 1) * head_dim || head_stride % 4 != 0) {
         set_error("noalloc decode: pos %d does not fit head_stride %lld (a multiple of 4 floats)",
                   pos, head_stride);
         return LEAP_ERR_INVALID;
