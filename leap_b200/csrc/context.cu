@@ -13,6 +13,10 @@
 #include <new>
 #include <vector>
 
+#include <mutex>
+#include <set>
+#include <utility>
+
 #include "ctx.h"
 
 namespace leap {
@@ -113,6 +117,22 @@ int cuda_status(cudaError_t e, const char *what) {
     cudaGetLastError();  // clear a non-sticky error
     set_error("%s: %s", what, cudaGetErrorString(e));
     return e == cudaErrorMemoryAllocation ? LEAP_ERR_NOMEM : LEAP_ERR_CUDA;
+}
+
+int set_kernel_smem(const void *fn, size_t bytes, const char *what, bool nonportable_cluster) {
+    static std::mutex mu;
+    static std::set<std::pair<const void *, int>> done;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_status(e, "cudaGetDevice");
+    std::lock_guard<std::mutex> lk(mu);
+    if (done.count({fn, dev})) return LEAP_OK;
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes));
+    if (e == cudaSuccess && nonportable_cluster)
+        e = cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return cuda_status(e, what);
+    done.insert({fn, dev});
+    return LEAP_OK;
 }
 
 }  // namespace leap

@@ -79,6 +79,13 @@ void clear_error();
 // Convert a CUDA error into a LEAP status (sets the message).
 int cuda_status(cudaError_t e, const char *what);
 
+// Opt kernel `fn` into `bytes` of dynamic shared memory on the current
+// device (and, with `nonportable_cluster`, into clusters above 8 CTAs).
+// Done once per (kernel, device) under a lock, so launches from several host
+// threads do not race.
+int set_kernel_smem(const void *fn, size_t bytes, const char *what,
+                    bool nonportable_cluster = false);
+
 inline float *k_head_ptr(const leap_ctx *c, int slot, int layer, int kvh) {
     return c->k_cache + slot * c->slot_stride + layer * c->layer_stride +
            kvh * c->head_stride;

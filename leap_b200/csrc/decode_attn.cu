@@ -558,15 +558,10 @@ template <int HD, int G, int SH>
 int launch_t(leap_ctx *c, const DecodeArgs &a, const DecodeSeq &tab, int total_splits,
              bool overlap, bool tail) {
     using C = Cfg<HD, G, SH>;
-    static bool attr_set[kMaxDevices] = {};  // the attribute is per device
-    if (c->device >= kMaxDevices) return cuda_status(cudaErrorInvalidDevice, "device");
-    if (!attr_set[c->device]) {
-        for (auto fn : {decode_attn_kernel<HD, G, SH, true>, decode_attn_kernel<HD, G, SH, false>}) {
-            cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 int(C::kSmem));
-            if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(decode)");
-        }
-        attr_set[c->device] = true;
+    for (auto fn : {decode_attn_kernel<HD, G, SH, true>, decode_attn_kernel<HD, G, SH, false>}) {
+        const int st = set_kernel_smem(reinterpret_cast<const void *>(fn), C::kSmem,
+                                       "cudaFuncSetAttribute(decode)");
+        if (st != LEAP_OK) return st;
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(total_splits, c->n_kv);

@@ -361,15 +361,9 @@ template <int HD, int G, int CS>
 int launch_c(leap_ctx *c, const ClusterArgs &a, const DecodeSeq &tab, bool overlap) {
     using C = CCfg<HD, G, CS>;
     auto kern = decode_cluster_kernel<HD, G, CS>;
-    static bool attr_set[kMaxDevices] = {};
-    if (!attr_set[c->device]) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             int(C::kSmem));
-        if (e == cudaSuccess && CS > 8)
-            e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-        if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(decode_cluster)");
-        attr_set[c->device] = true;
-    }
+    if (const int st = set_kernel_smem(reinterpret_cast<const void *>(kern), C::kSmem,
+                                       "cudaFuncSetAttribute(decode_cluster)", CS > 8))
+        return st;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(CS * tab.n_seq, c->n_kv);
     cfg.blockDim = dim3(kCThreads);

@@ -906,16 +906,6 @@ unsigned gemv_grid(const void *kernel, int items, size_t smem) {
     return unsigned(want < ctas ? want : ctas);
 }
 
-int set_smem_attr(const void *fn, bool *done, size_t bytes, const char *what) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (done[dev]) return LEAP_OK;
-    const cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               int(bytes));
-    if (e != cudaSuccess) return cuda_status(e, what);
-    done[dev] = true;
-    return LEAP_OK;
-}
 
 constexpr size_t kGemvSmemMax = 200 * 1024;
 
@@ -928,10 +918,9 @@ size_t gemv_q8_stream_smem(int n) {
 
 int gemv_q8_stream(cudaStream_t st, float *y, const int8_t *xq, const float *xs,
                    const int8_t *wq, const float *ws, int n, int d, const float *res, int *err) {
-    static bool attr[kMaxDevices] = {};
     const size_t smem = gemv_q8_stream_smem(n);
-    const int r = set_smem_attr(reinterpret_cast<const void *>(gemv_q8_stream_kernel), attr,
-                                kGemvSmemMax, "cudaFuncSetAttribute(gemv_q8_stream)");
+    const int r = set_kernel_smem(reinterpret_cast<const void *>(gemv_q8_stream_kernel),
+                                  kGemvSmemMax, "cudaFuncSetAttribute(gemv_q8_stream)");
     if (r != LEAP_OK) return r;
     int dev = 0, sms = 0, per_sm = 0;
     cudaGetDevice(&dev);
@@ -947,9 +936,8 @@ int gemv_q8_stream(cudaStream_t st, float *y, const int8_t *xq, const float *xs,
 
 int gemv_q8_slice(cudaStream_t st, float *y, const int8_t *xq, const float *xs, const int8_t *wq,
                   const float *ws, int n, int d, const float *res, size_t smem) {
-    static bool attr[kMaxDevices] = {};
-    const int r = set_smem_attr(reinterpret_cast<const void *>(gemv_q8_slice_kernel), attr,
-                                kGemvSmemMax, "cudaFuncSetAttribute(gemv_q8_slice)");
+    const int r = set_kernel_smem(reinterpret_cast<const void *>(gemv_q8_slice_kernel),
+                                  kGemvSmemMax, "cudaFuncSetAttribute(gemv_q8_slice)");
     if (r != LEAP_OK) return r;
     return launch_pdl("gemv_q8_slice", gemv_q8_slice_kernel, dim3(unsigned((d + kSR - 1) / kSR)),
                       dim3(256), smem, st, y, xq, xs, wq, ws, n, d, res);
@@ -969,8 +957,7 @@ int gemv_q8(cudaStream_t st, float *y, const int8_t *xq, const float *xs, const 
     if (g_q8_tma && gemv_q8_stream_smem(n) <= kGemvSmemMax)
         return gemv_q8_stream(st, y, xq, xs, wq, ws, n, d, res, err);
     if (g_q8_slice) return gemv_q8_slice(st, y, xq, xs, wq, ws, n, d, res, smem);
-    static bool attr[kMaxDevices] = {};
-    const int r = set_smem_attr(reinterpret_cast<const void *>(gemv_q8_kernel), attr, kGemvSmemMax,
+    const int r = set_kernel_smem(reinterpret_cast<const void *>(gemv_q8_kernel), kGemvSmemMax,
                                 "cudaFuncSetAttribute(gemv_q8)");
     if (r != LEAP_OK) return r;
     return launch_pdl("gemv_q8", gemv_q8_kernel, dim3(unsigned((d + kQR - 1) / kQR)),
@@ -992,8 +979,7 @@ int gemv_f32(cudaStream_t st, float *y, const float *x, const float *w, int n, i
         return LEAP_ERR_INVALID;
     }
     if (smem > kGemvSmemMax) return gemm_f32(st, y, x, w, n, d, 1, res);
-    static bool attr[kMaxDevices] = {};
-    const int r = set_smem_attr(reinterpret_cast<const void *>(gemv_f32_kernel), attr, kGemvSmemMax,
+    const int r = set_kernel_smem(reinterpret_cast<const void *>(gemv_f32_kernel), kGemvSmemMax,
                                 "cudaFuncSetAttribute(gemv_f32)");
     if (r != LEAP_OK) return r;
     const unsigned grid = gemv_grid(reinterpret_cast<const void *>(gemv_f32_kernel), d, smem);

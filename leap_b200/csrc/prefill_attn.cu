@@ -226,13 +226,8 @@ template <int HD, int G>
 int launch_fma(leap_ctx *c, const float *qrot, const float *kc, const float *vc, float *out,
                int pos0, int n_tok) {
     constexpr size_t smem = fma_smem_bytes<HD>();
-    static bool attr_set[kMaxDevices] = {};
-    if (!attr_set[c->device]) {
-        cudaError_t e = cudaFuncSetAttribute(prefill_fma_kernel<HD, G>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-        if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(prefill)");
-        attr_set[c->device] = true;
-    }
+    const void *fn = reinterpret_cast<const void *>(prefill_fma_kernel<HD, G>);
+    if (const int st = set_kernel_smem(fn, smem, "cudaFuncSetAttribute(prefill)")) return st;
     constexpr int BT = kBM / G;
     dim3 grid((n_tok + BT - 1) / BT, c->n_kv);
     prefill_fma_kernel<HD, G><<<grid, kPT, smem, c->stream>>>(

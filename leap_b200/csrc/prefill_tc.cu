@@ -344,13 +344,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) prefill_tc_kernel(const TcArgs 
 
 template <int G>
 int launch_tc_g(leap_ctx *c, const TcArgs &a) {
-    static bool attr_set[kMaxDevices] = {};
-    if (!attr_set[c->device]) {
-        const cudaError_t e = cudaFuncSetAttribute(
-            prefill_tc_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kTcSmem));
-        if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(prefill_tc)");
-        attr_set[c->device] = true;
-    }
+    const void *fn = reinterpret_cast<const void *>(prefill_tc_kernel<G>);
+    if (const int st = set_kernel_smem(fn, kTcSmem, "cudaFuncSetAttribute(prefill_tc)")) return st;
     constexpr int BT = kTcRows / G;
     dim3 grid((a.n_tok + BT - 1) / BT, c->n_kv);
     prefill_tc_kernel<G><<<grid, kTcThreads, kTcSmem, c->stream>>>(a);

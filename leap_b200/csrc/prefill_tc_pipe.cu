@@ -422,13 +422,8 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_tc_pipe_kernel(const PAr
 
 template <int G>
 int launch_pipe_g(leap_ctx *c, const PArgs &a) {
-    static bool attr_set[kMaxDevices] = {};
-    if (!attr_set[c->device]) {
-        const cudaError_t e = cudaFuncSetAttribute(
-            prefill_tc_pipe_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kPSmem));
-        if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(prefill_tc_pipe)");
-        attr_set[c->device] = true;
-    }
+    const void *fn = reinterpret_cast<const void *>(prefill_tc_pipe_kernel<G>);
+    if (const int st = set_kernel_smem(fn, kPSmem, "cudaFuncSetAttribute(prefill_tc_pipe)")) return st;
     constexpr int BT = kPRows / G;
     dim3 grid((a.n_tok + BT - 1) / BT, c->n_kv);
     prefill_tc_pipe_kernel<G><<<grid, kPThreads, kPSmem, c->stream>>>(a);

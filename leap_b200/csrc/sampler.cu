@@ -28,7 +28,6 @@
 // the coin or topp lies within that rounding of a running sum.
 #include <cmath>
 #include <cstdint>
-#include <mutex>
 
 #include "common.cuh"
 #include "ctx.h"
@@ -375,20 +374,10 @@ int sampler_launch(leap_sampler *s, cudaStream_t st, const float *logits, int *t
         set_error("sampler: device index out of range");
         return LEAP_ERR_INVALID;
     }
-    {
-        // The dynamic shared-memory opt-in is a per-device function attribute: set it once
-        // per device, under a lock so that samplers on several host threads do not race.
-        static std::mutex smem_attr_mu;
-        static bool smem_attr_set[kMaxDevices] = {};
-        std::lock_guard<std::mutex> lk(smem_attr_mu);
-        if (!smem_attr_set[s->device]) {
-            const cudaError_t e = cudaFuncSetAttribute(sample_kernel,
-                                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                       int(kSortCap * sizeof(uint64_t)));
-            if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(sample_kernel)");
-            smem_attr_set[s->device] = true;
-        }
-    }
+    if (const int r = set_kernel_smem(reinterpret_cast<const void *>(sample_kernel),
+                                      kSortCap * sizeof(uint64_t),
+                                      "cudaFuncSetAttribute(sample_kernel)"))
+        return r;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(1);
     cfg.blockDim = dim3(kSmpThreads);
