@@ -1,0 +1,74 @@
+"""Record the reference's own results for the end-to-end parity tests.
+
+Runs the reference build (``oracle/_ref``: the unmodified engine and its
+Sampler, compiled from the reference sources by ``oracle/Makefile``) on the
+same seeded inputs that ``tests/test_engine_gpu.py``,
+``tests/test_sampler_gpu.py`` and ``tests/test_support_ops_gpu.py`` build,
+and writes ``tests/golden/ref_fixtures.npz``.  Those tests use the
+recordings only where the reference build is absent (``tests/refsrc.py``).
+
+    python tests/golden/make_ref_fixtures.py
+
+Needs the reference build (``make -C oracle ref REF=<reference checkout>``
+or ``__graft_entry__.build()``); no GPU.
+"""
+from __future__ import annotations
+
+import json
+import os
+import sys
+import tempfile
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+TESTS = os.path.dirname(HERE)
+ROOT = os.path.dirname(TESTS)
+for p in (ROOT, TESTS):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+import oracle  # noqa: E402
+import refsrc  # noqa: E402
+import test_engine_gpu as te  # noqa: E402
+import test_sampler_gpu as ts  # noqa: E402
+import test_support_ops_gpu as to  # noqa: E402
+
+
+def main() -> None:
+    if not oracle.has_ref_engine():
+        raise SystemExit("the reference build (oracle/_ref) is missing: build it first")
+    out: dict[str, np.ndarray] = {}
+    with tempfile.TemporaryDirectory() as d:
+        paths = te.write_models(d)
+        for key, model, fmt, theta, prompt, steps in te.reference_runs():
+            ref = oracle.RefEngine(paths[(model, fmt)], theta_10k=(theta == 10000.0))
+            rec = refsrc.run_reference(ref, prompt, steps, full_every=refsrc.FULL_EVERY)
+            ref.close()
+            out.update(rec.arrays(key))
+            print(key, rec.steps, "steps", flush=True)
+        for model in te.MODELS:
+            for theta in (500000.0, 10000.0):
+                a, w = te.noise_floor_of(paths, model, theta)
+                out[te.noise_key(model, theta)] = np.asarray([a, w], np.float64)
+                print(te.noise_key(model, theta), a, w, flush=True)
+    for vocab, t, p in ts.CASES:
+        seed, logits = ts.case_inputs(vocab, t, p)
+        out[ts.sampler_key(vocab, t, p)] = ts.reference_draws(t, p, seed, logits).astype(np.int32)
+    _, t, p, seed = ts.FLAT
+    out["sampler_flat"] = ts.reference_draws(t, p, seed, ts.flat_inputs()).astype(np.int32)
+    out[ts.argmax_key("t0")] = np.asarray(oracle.ref_argmax(ts.peaked_logits()), np.int32)
+    for n, ties in to.ARGMAX_CASES:
+        out[to.argmax_case_key(n, ties)] = np.asarray(
+            oracle.ref_argmax(to.argmax_input(n, ties)), np.int32)
+    np.savez_compressed(refsrc.FIXTURE, **out)
+    with open(os.path.join(HERE, "ref_fixtures.json"), "w") as f:
+        json.dump({"generator": "tests/golden/make_ref_fixtures.py",
+                   "reference_build": "oracle/Makefile target ref (unmodified engine, Sampler)",
+                   "topk": refsrc.TOPK, "full_every": refsrc.FULL_EVERY,
+                   "keys": sorted(out)}, f, indent=1)
+    print("wrote", refsrc.FIXTURE, os.path.getsize(refsrc.FIXTURE), "bytes")
+
+
+if __name__ == "__main__":
+    main()

@@ -33,11 +33,14 @@ import pytest
 import torch
 
 import oracle
+import refsrc
 from leap_b200 import FLAG_NO_REPLY, LeapError, ModelConfig, Transformer
 from leap_b200.modelfile import write_v1, write_v2
 
-pytestmark = [pytest.mark.gpu,
-              pytest.mark.skipif(not oracle.has_ref_engine(), reason="oracle/_ref not built")]
+# The reference runs live where oracle/_ref is built, else from the recorded
+# results in tests/golden/ref_fixtures.npz (refsrc); with neither, the tests
+# fail rather than skip.
+pytestmark = pytest.mark.gpu
 
 MODELS = {
     # dim, hidden, layers, heads, kv heads, vocab, seq_len
@@ -60,22 +63,53 @@ def _perturbed_copy(path, dim, out):
     return out
 
 
-@pytest.fixture(scope="module")
-def model_files(tmp_path_factory):
-    d = tmp_path_factory.mktemp("models")
+def write_models(d):
+    """The seeded model files of this module (also used by the fixture
+    recorder, tests/golden/make_ref_fixtures.py)."""
     out = {}
     for name, cfg in MODELS.items():
         for fmt, writer in (("v1", write_v1), ("v2", write_v2)):
-            p = str(d / f"{name}_{fmt}.bin")
+            p = os.path.join(str(d), f"{name}_{fmt}.bin")
             writer(p, cfg, seed=0)
             out[(name, fmt)] = p
         out[(name, "v2+ulp")] = _perturbed_copy(out[(name, "v2")], cfg.dim,
-                                                str(d / f"{name}_v2_ulp.bin"))
+                                                os.path.join(str(d), f"{name}_v2_ulp.bin"))
     return out
+
+
+@pytest.fixture(scope="module")
+def model_files(tmp_path_factory):
+    return write_models(tmp_path_factory.mktemp("models"))
 
 
 def _prompt(n, vocab, seed=0):
     return [int(t) for t in np.random.default_rng(seed).integers(0, vocab, n)]
+
+
+def engine_key(model, fmt, theta):
+    return f"engine/{model}/{fmt}/{theta:g}"
+
+
+def batched_key(fmt):
+    return f"engine_batched/{fmt}"
+
+
+def noise_key(model, theta):
+    return f"noise/{model}/{theta:g}"
+
+
+# (key, model, format, theta, prompt, steps) of every reference run below
+def reference_runs():
+    runs = []
+    for model, cfg in MODELS.items():
+        for fmt in ("v1", "v2"):
+            for theta in (500000.0, 10000.0):
+                runs.append((engine_key(model, fmt, theta), model, fmt, theta,
+                             _prompt(32, cfg.vocab_size), STEPS[model]))
+    for fmt in ("v1", "v2"):
+        runs.append((batched_key(fmt), "hd128", fmt, 500000.0,
+                     _prompt(150, MODELS["hd128"].vocab_size, seed=1), 64))
+    return runs
 
 
 class _RefAsEngine:
@@ -90,51 +124,60 @@ class _RefAsEngine:
         return lg
 
 
-def _teacher_forced(ref, eng, prompt, steps, batched_prompt=False, check_ties=True):
-    """(agreement, worst logits error / max|logits|) of `eng` against `ref`,
-    both fed the reference's greedy tokens."""
-    vocab = ref.config[5]
-    for p, t in enumerate(prompt[:-1]):
-        ref.forward(t, p)
+def _teacher_forced(rec, eng, prompt, steps, batched_prompt=False, check_ties=True):
+    """(agreement, worst logits error / max|logits|) of `eng` against the
+    reference run `rec` (refsrc.EngineRecord), both fed the reference's
+    greedy tokens."""
     if batched_prompt:
         eng.prefill(prompt[:-1], 0)
     else:
         for p, t in enumerate(prompt[:-1]):
             eng.forward(t, p, FLAG_NO_REPLY)
     tok, pos = prompt[-1], len(prompt) - 1
+    vocab = next(iter(rec.full.values())).size
     agree, worst = 0, 0.0
-    for _ in range(steps):
-        lr = ref.forward(tok, pos)
+    for i in range(steps):
         le = eng.forward(tok, pos)
         assert le.shape == (vocab,) and np.isfinite(le).all()
-        scale = float(np.abs(lr).max())
-        err = float(np.abs(le - lr).max())
-        worst = max(worst, err / scale)
-        r_tok = ref.argmax(lr)
-        if eng.last_token == r_tok:
+        same, err, margin, comparable = refsrc.compare_step(rec, i, le, eng.last_token)
+        worst = max(worst, err / float(rec.scale[i]))
+        if same:
             agree += 1
         elif check_ties:
-            top2 = np.sort(lr)[-2:]
-            assert top2[1] - top2[0] <= 2 * err, (
+            assert comparable and margin <= 2 * err, (
                 f"top-1 differs at pos {pos} where the reference is not near a tie")
-        tok, pos = r_tok, pos + 1
+        tok, pos = int(rec.ref_tok[i]), pos + 1
     return agree / steps, worst
+
+
+def noise_floor_of(paths, model, theta):
+    """The reference engine against itself with one-ulp norm perturbations
+    (live): (agreement, worst error) on the W8A8 file."""
+    cfg = MODELS[model]
+    t10 = theta == 10000.0
+    a = oracle.RefEngine(paths[(model, "v2")], theta_10k=t10)
+    b = oracle.RefEngine(paths[(model, "v2+ulp")], theta_10k=t10)
+    try:
+        prompt = _prompt(32, cfg.vocab_size)
+        rec = refsrc.run_reference(a, prompt, STEPS[model])
+        return _teacher_forced(rec, _RefAsEngine(b), prompt, STEPS[model], check_ties=False)
+    finally:
+        a.close()
+        b.close()
 
 
 @pytest.fixture(scope="module")
 def noise_floor(model_files):
-    """The reference engine against itself with one-ulp norm perturbations:
-    {(model, theta): (agreement, worst error)} on the W8A8 files."""
+    """{(model, theta): (agreement, worst error)} of the reference against
+    itself on the W8A8 files: live, or recorded."""
     out = {}
-    for model, cfg in MODELS.items():
+    for model in MODELS:
         for theta in (500000.0, 10000.0):
-            t10 = theta == 10000.0
-            a = oracle.RefEngine(model_files[(model, "v2")], theta_10k=t10)
-            b = oracle.RefEngine(model_files[(model, "v2+ulp")], theta_10k=t10)
-            out[(model, theta)] = _teacher_forced(a, _RefAsEngine(b), _prompt(32, cfg.vocab_size),
-                                                  STEPS[model], check_ties=False)
-            a.close()
-            b.close()
+            if refsrc.live():
+                out[(model, theta)] = noise_floor_of(model_files, model, theta)
+            else:
+                a, w = refsrc.recorded(noise_key(model, theta))
+                out[(model, theta)] = (float(a), float(w))
     return out
 
 
@@ -154,11 +197,11 @@ def _accept(fmt, agree, worst, floor):
 def test_teacher_forced_against_reference_engine(cuda, model_files, noise_floor, model, fmt,
                                                  theta):
     path = model_files[(model, fmt)]
-    ref = oracle.RefEngine(path, theta_10k=(theta == 10000.0))
+    prompt = _prompt(32, MODELS[model].vocab_size)
+    rec = refsrc.engine_reference(engine_key(model, fmt, theta), path, theta == 10000.0, prompt,
+                                  STEPS[model])
     with Transformer.create(path, rope_theta=theta, max_chunk=64) as eng:
-        prompt = _prompt(32, MODELS[model].vocab_size)
-        agree, worst = _teacher_forced(ref, eng, prompt, STEPS[model])
-    ref.close()
+        agree, worst = _teacher_forced(rec, eng, prompt, STEPS[model])
     print(f"{model} {fmt} theta {theta:g}: agree {agree:.4f} worst {worst:.3g} "
           f"(reference self: {noise_floor[(model, theta)]})")
     _accept(fmt, agree, worst, noise_floor[(model, theta)])
@@ -169,11 +212,10 @@ def test_batched_prompt_against_reference_engine(cuda, model_files, noise_floor,
     """The prompt goes through the chunked path (GEMM projections + causal
     prefill attention, 64-token chunks with a ragged last chunk)."""
     path = model_files[("hd128", fmt)]
-    ref = oracle.RefEngine(path)
+    prompt = _prompt(150, MODELS["hd128"].vocab_size, seed=1)
+    rec = refsrc.engine_reference(batched_key(fmt), path, False, prompt, 64)
     with Transformer.create(path, max_chunk=64) as eng:
-        prompt = _prompt(150, MODELS["hd128"].vocab_size, seed=1)
-        agree, worst = _teacher_forced(ref, eng, prompt, 64, batched_prompt=True)
-    ref.close()
+        agree, worst = _teacher_forced(rec, eng, prompt, 64, batched_prompt=True)
     _accept(fmt, agree, worst, noise_floor[("hd128", 500000.0)])
 
 

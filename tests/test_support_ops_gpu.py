@@ -15,6 +15,7 @@ import pytest
 import torch
 
 import oracle
+import refsrc
 from leap_b200._native import LeapError, check, lib
 
 pytestmark = pytest.mark.gpu
@@ -190,17 +191,30 @@ def _lane_order_argmax(v):
     return best
 
 
-@pytest.mark.parametrize("n,ties", [(1, []), (7, [2, 5]), (32000, [9, 16]),
-                                    (32000, [15, 8, 31999]), (128256, [17, 90, 128255]),
-                                    (32003, [32001, 31999])])
-def test_argmax_reference_tie_order(cuda, n, ties):
+ARGMAX_CASES = [(1, []), (7, [2, 5]), (32000, [9, 16]), (32000, [15, 8, 31999]),
+                (128256, [17, 90, 128255]), (32003, [32001, 31999])]
+
+
+def argmax_input(n, ties):
     r = np.random.default_rng(n + len(ties))
     v = r.standard_normal(n).astype(np.float32)
     if ties:
         v[ties] = v.max() + 1
+    return v
+
+
+def argmax_case_key(n, ties):
+    return "argmax/" + "_".join(str(x) for x in [n] + list(ties))
+
+
+@pytest.mark.parametrize("n,ties", ARGMAX_CASES)
+def test_argmax_reference_tie_order(cuda, n, ties):
+    """The reference Sampler's argmax (live, or its recorded answer)."""
+    v = argmax_input(n, ties)
     tok = torch.empty(1, dtype=torch.int32, device="cuda")
     check(lib().leap_op_argmax(_s(), tok.data_ptr(), _dev(v).data_ptr(), n))
-    want = oracle.ref_argmax(v) if oracle.has_ref_engine() else _lane_order_argmax(v)
+    want = (oracle.ref_argmax(v) if refsrc.live()
+            else int(refsrc.recorded(argmax_case_key(n, ties))))
     assert int(tok.item()) == want == _lane_order_argmax(v)
 
 
