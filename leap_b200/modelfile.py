@@ -18,12 +18,17 @@ Layouts follow the reference exporter and loader:
   ``q = round_half_away(w * (1/s))``.
 
 Synthetic weights are N(0, 0.02) from ``numpy.random.default_rng`` seeded per
-tensor, RMSNorm weights 1.0 — the BASELINE configs' description.
+tensor (tensors above 64M elements per 16M-element block), RMSNorm weights
+1.0 — the BASELINE configs' description.  Blocks are generated and quantized
+on a thread pool (numpy releases the GIL in both), so multi-GB files take
+seconds to a few minutes; the bytes do not depend on the thread count.
 """
 from __future__ import annotations
 
+import concurrent.futures as cf
 import dataclasses
 import hashlib
+import os
 import struct
 
 import numpy as np
@@ -92,8 +97,7 @@ def _normal(seed, name, shape, std=0.02):
     return (_rng(seed, name).standard_normal(shape, dtype=np.float32) * np.float32(std))
 
 
-def quantize_q80(w: np.ndarray, gs: int):
-    """src/export/Utils.cpp:58-85 on a flat float32 array."""
+def _quantize_block(w: np.ndarray, gs: int):
     g = w.reshape(-1, gs)
     wmax = np.abs(g).max(axis=1).astype(np.float32)
     s = (wmax / np.float32(127.0)).astype(np.float32)
@@ -101,6 +105,84 @@ def quantize_q80(w: np.ndarray, gs: int):
     v = (g * inv[:, None].astype(np.float32)).astype(np.float32)
     q = (np.sign(v) * np.floor(np.abs(v) + np.float32(0.5))).astype(np.int8)
     return q.reshape(-1), s
+
+
+def quantize_q80(w: np.ndarray, gs: int):
+    """src/export/Utils.cpp:58-85 on a flat float32 array: per group of `gs`,
+    s = max|w| / 127 and q = round-half-away-from-zero(w * (1/s)), all in
+    float32.  Worked in 1M-element pieces so the temporaries stay in cache."""
+    w = w.reshape(-1)
+    piece = (1 << 20) // gs * gs
+    if w.size <= piece:
+        return _quantize_block(w, gs)
+    q = np.empty(w.size, np.int8)
+    s = np.empty(w.size // gs, np.float32)
+    for a in range(0, w.size, piece):
+        qa, sa = _quantize_block(w[a:a + piece], gs)
+        q[a:a + qa.size] = qa
+        s[a // gs:a // gs + sa.size] = sa
+    return q, s
+
+
+_BIG = 1 << 26    # tensors above this many elements are seeded per block
+_BLOCK = 1 << 24  # elements per block of a big tensor
+
+
+def _blocks(name: str, numel: int):
+    """(rng name, element count) of each seeded block of a tensor, in order."""
+    if numel <= _BIG:
+        return [(name, numel)]
+    return [(f"{name}#{i}", min(_BLOCK, numel - a)) for i, a in enumerate(range(0, numel, _BLOCK))]
+
+
+def _threads() -> int:
+    return max(1, min(32, os.cpu_count() or 1))
+
+
+def _write_tensors(f, items, seed: int, quant_gs: int = 0) -> None:
+    """Write each (name, shape) tensor of `items` in order: FP32, or (with
+    quant_gs) its int8 codes followed by its float32 group scales."""
+    jobs = []
+    for name, shape in items:
+        numel = int(np.prod(shape))
+        for bname, n in _blocks(name, numel):
+            jobs.append((name, bname, n))
+
+    def make(job):
+        _, bname, n = job
+        w = _normal(seed, bname, (n,))
+        return quantize_q80(w, quant_gs) if quant_gs else w
+
+    pending_scales: list[np.ndarray] = []
+    current = None
+    nt = _threads()
+    with cf.ThreadPoolExecutor(max_workers=nt) as ex:
+        window = []
+        it = iter(jobs)
+
+        def refill():
+            for job in it:
+                window.append((job, ex.submit(make, job)))
+                if len(window) >= 2 * nt:
+                    break
+        refill()
+        while window:
+            job, fut = window.pop(0)
+            res = fut.result()
+            refill()
+            name = job[0]
+            if quant_gs:
+                if current is not None and name != current:
+                    for sc in pending_scales:
+                        f.write(sc.tobytes())
+                    pending_scales = []
+                current = name
+                f.write(res[0].tobytes())
+                pending_scales.append(res[1])
+            else:
+                f.write(res.tobytes())
+    for sc in pending_scales:
+        f.write(sc.tobytes())
 
 
 def _tensors(cfg: ModelConfig, seed: int):
@@ -122,9 +204,7 @@ def write_v1(path: str, cfg: ModelConfig, seed: int = 0) -> None:
         ones = np.ones(cfg.dim, np.float32)
         for _ in range(2 * cfg.n_layers + 1):
             f.write(ones.tobytes())
-        f.write(_normal(seed, "tok", (cfg.vocab_size, cfg.dim)).tobytes())
-        for name, shape in _tensors(cfg, seed):
-            f.write(_normal(seed, name, shape).tobytes())
+        _write_tensors(f, [("tok", (cfg.vocab_size, cfg.dim))] + _tensors(cfg, seed), seed)
 
 
 def write_v2(path: str, cfg: ModelConfig, seed: int = 0, group_size: int = 64) -> None:
@@ -136,10 +216,8 @@ def write_v2(path: str, cfg: ModelConfig, seed: int = 0, group_size: int = 64) -
         ones = np.ones(cfg.dim, np.float32)
         for _ in range(2 * cfg.n_layers + 1):
             f.write(ones.tobytes())
-        for name, shape in [("tok", (cfg.vocab_size, cfg.dim))] + _tensors(cfg, seed):
-            q, s = quantize_q80(_normal(seed, name, shape).reshape(-1), group_size)
-            f.write(q.tobytes())
-            f.write(s.tobytes())
+        _write_tensors(f, [("tok", (cfg.vocab_size, cfg.dim))] + _tensors(cfg, seed), seed,
+                       quant_gs=group_size)
 
 
 def write_timing_file(path: str, cfg: ModelConfig, quantized: bool, group_size: int = 64,

@@ -7,10 +7,14 @@ same seeded inputs that ``tests/test_engine_gpu.py``,
 and writes ``tests/golden/ref_fixtures.npz``.  Those tests use the
 recordings only where the reference build is absent (``tests/refsrc.py``).
 
-    python tests/golden/make_ref_fixtures.py
+    python tests/golden/make_ref_fixtures.py [--part small|configs|all]
 
-Needs the reference build (``make -C oracle ref REF=<reference checkout>``
-or ``__graft_entry__.build()``); no GPU.
+``small`` records the cases of the small models and the sampler, ``configs``
+the BASELINE-shaped files of ``tests/test_configs_e2e_gpu.py`` (a 4 GB and
+an 8 GB model file in a temporary directory; several minutes); other keys
+already in the file are kept.  Needs the reference build
+(``make -C oracle ref REF=<reference checkout>`` or
+``__graft_entry__.build()``); no GPU.
 """
 from __future__ import annotations
 
@@ -30,15 +34,53 @@ for p in (ROOT, TESTS):
 
 import oracle  # noqa: E402
 import refsrc  # noqa: E402
+import test_configs_e2e_gpu as tc  # noqa: E402
 import test_engine_gpu as te  # noqa: E402
 import test_sampler_gpu as ts  # noqa: E402
 import test_support_ops_gpu as to  # noqa: E402
 
 
+FIRST_AND_LAST = 1 << 30  # full logits at the first and last step only
+
+
+def record_configs(out: dict) -> None:
+    with tempfile.TemporaryDirectory() as d:
+        p1 = tc.write_config1(d)
+        prompt = te._prompt(tc.TL_PROMPT, tc.TL.vocab_size, seed=0)
+        for theta in (10000.0, 500000.0):
+            ref = oracle.RefEngine(p1, theta_10k=(theta == 10000.0))
+            rec = refsrc.run_reference(ref, prompt, tc.TL_STEPS, full_every=FIRST_AND_LAST)
+            ref.close()
+            out.update(rec.arrays(tc.config1_key(theta)))
+            print(tc.config1_key(theta), flush=True)
+        os.remove(p1)
+        p5, q5 = tc.write_config5(d)
+        prompt = te._prompt(tc.L70_PROMPT, tc.L70.vocab_size, seed=0)
+        ref = oracle.RefEngine(p5)
+        rec = refsrc.run_reference(ref, prompt, tc.L70_STEPS, full_every=FIRST_AND_LAST)
+        ref.close()
+        out.update(rec.arrays(tc.CONFIG5_KEY))
+        a, w = tc.config5_noise(p5, q5, prompt)
+        out[tc.CONFIG5_NOISE_KEY] = np.asarray([a, w], np.float64)
+        print(tc.CONFIG5_KEY, "noise", a, w, flush=True)
+
+
 def main() -> None:
+    import argparse
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--part", choices=["small", "configs", "all"], default="all")
+    part = ap.parse_args().part
     if not oracle.has_ref_engine():
         raise SystemExit("the reference build (oracle/_ref) is missing: build it first")
     out: dict[str, np.ndarray] = {}
+    if os.path.exists(refsrc.FIXTURE):
+        with np.load(refsrc.FIXTURE) as z:
+            out.update({k: z[k] for k in z.files})
+    if part in ("configs", "all"):
+        record_configs(out)
+    if part == "configs":
+        save(out)
+        return
     with tempfile.TemporaryDirectory() as d:
         paths = te.write_models(d)
         for key, model, fmt, theta, prompt, steps in te.reference_runs():
@@ -61,6 +103,10 @@ def main() -> None:
     for n, ties in to.ARGMAX_CASES:
         out[to.argmax_case_key(n, ties)] = np.asarray(
             oracle.ref_argmax(to.argmax_input(n, ties)), np.int32)
+    save(out)
+
+
+def save(out: dict) -> None:
     np.savez_compressed(refsrc.FIXTURE, **out)
     with open(os.path.join(HERE, "ref_fixtures.json"), "w") as f:
         json.dump({"generator": "tests/golden/make_ref_fixtures.py",

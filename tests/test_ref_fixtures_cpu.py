@@ -10,6 +10,7 @@ import pytest
 
 import oracle
 import refsrc
+import test_configs_e2e_gpu as tc
 import test_engine_gpu as te
 import test_sampler_gpu as ts
 import test_support_ops_gpu as to
@@ -26,6 +27,10 @@ def test_every_recording_the_gpu_tests_read_exists():
     keys |= {ts.sampler_key(*c) for c in ts.CASES}
     keys |= {"sampler_flat", ts.argmax_key("t0")}
     keys |= {to.argmax_case_key(n, t) for n, t in to.ARGMAX_CASES}
+    for key in [tc.config1_key(10000.0), tc.config1_key(500000.0), tc.CONFIG5_KEY]:
+        keys |= {f"{key}/{f}" for f in ("ref_tok", "top_idx", "top_val", "scale",
+                                         "full_steps", "full")}
+    keys.add(tc.CONFIG5_NOISE_KEY)
     for k in sorted(keys):
         refsrc.recorded(k)
     rec = refsrc.EngineRecord.load(te.engine_key("hd64", "v1", 500000.0))
