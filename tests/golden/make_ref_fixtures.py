@@ -57,10 +57,13 @@ def record_configs(out: dict) -> None:
         p5, q5 = tc.write_config5(d)
         prompt = te._prompt(tc.L70_PROMPT, tc.L70.vocab_size, seed=0)
         ref = oracle.RefEngine(p5)
-        rec = refsrc.run_reference(ref, prompt, tc.L70_STEPS, full_every=FIRST_AND_LAST)
+        full = refsrc.run_reference(ref, prompt, tc.L70_STEPS)
         ref.close()
+        rec = refsrc.EngineRecord(full.ref_tok, full.top_idx, full.top_val, full.scale,
+                                  [0, tc.L70_STEPS - 1],
+                                  [full.full[0], full.full[tc.L70_STEPS - 1]])
         out.update(rec.arrays(tc.CONFIG5_KEY))
-        a, w = tc.config5_noise(p5, q5, prompt)
+        a, w = tc.config5_noise(full, q5, prompt)
         out[tc.CONFIG5_NOISE_KEY] = np.asarray([a, w], np.float64)
         print(tc.CONFIG5_KEY, "noise", a, w, flush=True)
 
