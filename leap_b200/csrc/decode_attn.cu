@@ -32,7 +32,9 @@ namespace {
 //   0: 128 threads, 16 KB tiles, two CTAs per SM;
 //   1: 256 threads, 32 KB tiles, one CTA per SM (half as many splits).
 constexpr int kStages = 3;
+constexpr int kEarlyStages = 2;  // stages filled before the dependency wait
 constexpr int kMaxSplitsPerSeq = 256;
+constexpr float kRescaleLog2 = 8.f;  // see the online softmax in the tile loop
 
 template <int HD, int G, int SH>
 struct Cfg {
@@ -128,20 +130,28 @@ decode_attn_kernel(const DecodeArgs a, const DecodeSeq tab) {
     }
     __syncthreads();
 
-    if (tid == 0) {
-        for (int t = 0; t < min(kStages, n_tiles); ++t) {
-            const int r0 = row_begin + t * C::TILE;
-            const uint32_t bytes = min(C::TILE, row_end - r0) * HD * 4;
-            mbar_arrive_expect_tx(&full_bar[t], 2 * bytes);
-            bulk_g2s(sK + t * C::TILE * HD, gK + size_t(r0) * HD, bytes, &full_bar[t]);
-            bulk_g2s(sV + t * C::TILE * HD, gV + size_t(r0) * HD, bytes, &full_bar[t]);
-        }
-    }
+    // Stage the first tiles: kEarlyStages of them before the dependency wait
+    // (they overlap the previous kernel's tail), the rest after it.  Filling
+    // every stage early was measured slower: those copies compete with the
+    // previous kernel's split-KV combine, which is on the critical path.
+    auto stage_tile = [&](int t) {
+        const int r0 = row_begin + t * C::TILE;
+        const uint32_t bytes = min(C::TILE, row_end - r0) * HD * 4;
+        mbar_arrive_expect_tx(&full_bar[t % kStages], 2 * bytes);
+        bulk_g2s(sK + (t % kStages) * C::TILE * HD, gK + size_t(r0) * HD, bytes,
+                 &full_bar[t % kStages]);
+        bulk_g2s(sV + (t % kStages) * C::TILE * HD, gV + size_t(r0) * HD, bytes,
+                 &full_bar[t % kStages]);
+    };
+    if (tid == 0)
+        for (int t = 0; t < min(kEarlyStages, n_tiles); ++t) stage_tile(t);
     // Up to here only this layer's cache rows were read, which the previous
     // kernel of the stream never writes (the host launches with overlap only
     // then).  Inputs, scratch and outputs may still be in use by it.
     grid_dependency_wait();
     grid_launch_dependents();
+    if (tid == 0)
+        for (int t = kEarlyStages; t < min(kStages, n_tiles); ++t) stage_tile(t);
 
     // ---- rotated q slice: heads kvh*G .. +G, dims of this lane's chunks ---
     const int qh0 = kvh * G;
@@ -176,21 +186,24 @@ decode_attn_kernel(const DecodeArgs a, const DecodeSeq tab) {
     }
 
     // ---- main loop over tiles --------------------------------------------
-    bool ok = true;
-    int t = 0;
-    for (; t < n_tiles; ++t) {
-        const int s = t % kStages;
-        ok = mbar_wait(&full_bar[s], (t / kStages) & 1);
-        ok = __syncthreads_and(ok);
-        if (!ok) break;
-        const int r0 = row_begin + t * C::TILE;
-        float *tK = sK + s * C::TILE * HD;
-        float *tV = sV + s * C::TILE * HD;
+    // Tile by tile: wait, scores, softmax update and V sum, then release the
+    // stage for the refill.  (Forming the scores of tile t+1 alongside the V
+    // sum of tile t was measured slower: at the dependency release every
+    // stage is full and no copy is in flight until the first stage is
+    // released, so that release must come as early as possible.)
 
+    // Wait for tile tt; if it holds row `pos`, rotate k, append k and v to
+    // the cache, and patch the staged tile (the copy may have read the old
+    // row).  False if the wait gave up.
+    auto tile_ready = [&](int tt) -> bool {
+        bool r = mbar_wait(&full_bar[tt % kStages], (tt / kStages) & 1);
+        r = __syncthreads_and(r);
+        if (!r) return false;
+        const int r0 = row_begin + tt * C::TILE;
         if (last_split && pos < r0 + C::TILE) {
-            // the new token's row: rotate k, append k and v to the cache,
-            // and patch the staged tile (the copy may have read the old row)
             const int rr = pos - r0;
+            float *tK = sK + (tt % kStages) * C::TILE * HD;
+            float *tV = sV + (tt % kStages) * C::TILE * HD;
             const float *kn = a.k_new + (size_t(seq) * a.n_kv + kvh) * HD;
             const float *vn = a.v_new + (size_t(seq) * a.n_kv + kvh) * HD;
             for (int d = 2 * tid; d < HD; d += 2 * C::THREADS) {
@@ -204,8 +217,14 @@ decode_attn_kernel(const DecodeArgs a, const DecodeSeq tab) {
             }
             __syncthreads();
         }
+        return true;
+    };
 
-        float sc[C::RPG][G];
+    // Scaled scores (log2 units) of this lane group's rows of tile tt;
+    // -inf beyond the split.
+    auto tile_scores = [&](int tt, float (&sc)[C::RPG][G]) {
+        const int r0 = row_begin + tt * C::TILE;
+        const float *tK = sK + (tt % kStages) * C::TILE * HD;
 #pragma unroll
         for (int rr = 0; rr < C::RPG; ++rr) {
             const int row = rr * C::NGRP + grp;
@@ -237,18 +256,35 @@ decode_attn_kernel(const DecodeArgs a, const DecodeSeq tab) {
 #pragma unroll
             for (int g = 0; g < G; ++g) sc[rr][g] = valid ? acc[g] * a.scale_log2 : -INFINITY;
         }
+    };
 
-        // online softmax update over this tile's rows of the group
+    // Online softmax update and weighted V sum of tile tt.  The running max m
+    // (log2 units) is a lazily moved reference: it moves, and l and o are
+    // rescaled, only when a score exceeds it by more than kRescaleLog2, so
+    // p = 2^(s - m) <= 2^8.  Exact in real arithmetic; after the first tile
+    // it is rarely taken.
+    auto tile_accumulate = [&](int tt, const float (&sc)[C::RPG][G]) {
+        const int r0 = row_begin + tt * C::TILE;
+        const float *tV = sV + (tt % kStages) * C::TILE * HD;
+        float mt[G];
+        bool grow = false;
 #pragma unroll
         for (int g = 0; g < G; ++g) {
-            float mt = m[g];
+            mt[g] = sc[0][g];
 #pragma unroll
-            for (int rr = 0; rr < C::RPG; ++rr) mt = fmaxf(mt, sc[rr][g]);
-            const float alpha = (mt == -INFINITY) ? 1.f : fast_exp2(m[g] - mt);
-            m[g] = mt;
-            l[g] *= alpha;
+            for (int rr = 1; rr < C::RPG; ++rr) mt[g] = fmaxf(mt[g], sc[rr][g]);
+            grow |= mt[g] > m[g] + kRescaleLog2;
+        }
+        if (__any_sync(0xffffffffu, grow)) {
 #pragma unroll
-            for (int d = 0; d < C::DPL; ++d) o[g][d] *= alpha;
+            for (int g = 0; g < G; ++g) {
+                const float mn = fmaxf(m[g], mt[g]);
+                const float alpha = (mn == -INFINITY) ? 1.f : fast_exp2(m[g] - mn);
+                m[g] = mn;
+                l[g] *= alpha;
+#pragma unroll
+                for (int d = 0; d < C::DPL; ++d) o[g][d] *= alpha;
+            }
         }
 #pragma unroll
         for (int rr = 0; rr < C::RPG; ++rr) {
@@ -275,22 +311,30 @@ decode_attn_kernel(const DecodeArgs a, const DecodeSeq tab) {
                 }
             }
         }
+    };
 
-        __syncthreads();  // every warp is done with stage s
-        if (tid == 0 && t + kStages < n_tiles) {
-            const int tn = t + kStages;
-            const int rn = row_begin + tn * C::TILE;
-            const uint32_t bytes = min(C::TILE, row_end - rn) * HD * 4;
-            mbar_arrive_expect_tx(&full_bar[s], 2 * bytes);
-            bulk_g2s(tK, gK + size_t(rn) * HD, bytes, &full_bar[s]);
-            bulk_g2s(tV, gV + size_t(rn) * HD, bytes, &full_bar[s]);
+    // Every warp is done with tile tt's stage: refill it with tile tt+kStages.
+    auto tile_release = [&](int tt) {
+        __syncthreads();
+        if (tid == 0 && tt + kStages < n_tiles) stage_tile(tt + kStages);
+    };
+
+    int failed = -1;  // the tile whose wait gave up
+    for (int t = 0; t < n_tiles; ++t) {
+        if (!tile_ready(t)) {
+            failed = t;
+            break;
         }
+        float sc[C::RPG][G];
+        tile_scores(t, sc);
+        tile_accumulate(t, sc);
+        tile_release(t);
     }
 
-    if (!ok) {
+    if (failed >= 0) {
         // A wait gave up: give the copies still in flight a bounded chance
         // to land before this CTA's shared memory is released, then report.
-        for (int tt = t + 1; tt < min(t + kStages, n_tiles); ++tt)
+        for (int tt = failed + 1; tt < min(failed + kStages, n_tiles); ++tt)
             (void)mbar_wait(&full_bar[tt % kStages], (tt / kStages) & 1);
         if (tid == 0) report_error(a.err, kDevWaitTimeout);
         return;
@@ -305,16 +349,20 @@ decode_attn_kernel(const DecodeArgs a, const DecodeSeq tab) {
         }
     }
     __syncthreads();
-    if (tid < G) {
-        float M = -INFINITY;
-        for (int gg = 0; gg < C::NGRP; ++gg) M = fmaxf(M, red_m[gg][tid]);
-        float L = 0.f;
-        for (int gg = 0; gg < C::NGRP; ++gg) {
-            const float mg = red_m[gg][tid];
-            if (mg != -INFINITY) L += red_l[gg][tid] * fast_exp2(mg - M);
+    // one warp per head: lane k holds row group k's (m, l) (NGRP <= 32)
+    static_assert(C::NGRP <= 32, "one lane per row group");
+    for (int g = warp; g < G; g += C::WARPS) {
+        const float mg = lane < C::NGRP ? red_m[lane][g] : -INFINITY;
+        float M = mg;
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+        float L = mg != -INFINITY ? red_l[lane][g] * fast_exp2(mg - M) : 0.f;
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+        if (lane == 0) {
+            s_M[g] = M;
+            s_L[g] = L;
         }
-        s_M[tid] = M;
-        s_L[tid] = L;
     }
     __syncthreads();
     float *red_o = sK;  // [NGRP][G][HD]; the pipeline is drained
@@ -448,6 +496,7 @@ decode_attn_kernel(const DecodeArgs a, const DecodeSeq tab) {
             const int e = tid + r * C::THREADS;
             if (e < C::NV4) {
                 const int g = (4 * e) / HD;
+#pragma unroll 8
                 for (int i = 0; i < n; ++i) {
                     const float w = cW[(s0 + i) * G + g];
                     const float4 v = *reinterpret_cast<const float4 *>(sO + i * G * HD + 4 * e);
@@ -595,9 +644,11 @@ int launch_t(leap_ctx *c, const DecodeArgs &a, const DecodeSeq &tab, int total_s
 }  // namespace
 
 int plan_decode(const leap_ctx *c, DecodeSeq &tab, int shape) {
-    const int tile_bytes = shape == 1 ? 32768 : 16384;
     const int per_sm = shape == 1 ? 1 : 2;
-    const long cap_rows = 16L * tile_bytes / (c->hd * 4 * 2);  // 256/512 KB of K+V per CTA
+    // At most 1024 rows (4 MB of K+V at head_dim 128) per CTA: long splits
+    // amortise each CTA's prologue and partial; launches that fit one wave
+    // are split finer anyway (below).
+    const long cap_rows = 1024L * 128 / c->hd;
     long total = 0;
     int max_ctx = 0;
     for (int i = 0; i < tab.n_seq; ++i) {
@@ -632,7 +683,9 @@ int plan_decode(const leap_ctx *c, DecodeSeq &tab, int shape) {
 }
 
 int max_decode_parts(int hd, int n_kv, int max_batch, int max_seq_pad, int num_sms) {
-    const long cap_rows = 262144L / (hd * 4 * 2);  // the narrow CTA shape needs most
+    // An upper bound on plan_decode's CTA count: a chunk shorter than 256
+    // rows (hd 128) only occurs when the launch fits one wave (2 per SM).
+    const long cap_rows = 262144L / (hd * 4 * 2);
     const long nb = max_batch < kMaxSeqPerLaunch ? max_batch : kMaxSeqPerLaunch;
     long a = (nb * max_seq_pad * long(n_kv) + cap_rows - 1) / cap_rows;
     if (a < 2L * num_sms) a = 2L * num_sms;
