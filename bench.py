@@ -424,6 +424,18 @@ def run_gpu_arm(args):
             "clocks": clocks,
         }
     ctx.close()
+    del q, kn, vn, out
+    torch.cuda.empty_cache()
+    if not args.no_pipeline:
+        # The split that shards: the Llama-3-8B-shape W8A8 model as N
+        # layer-range stages, one per rank (BASELINE metric "tok/s
+        # Llama-3-8B-shape W8A8 at 1/2/4/8 GPU"); outside the timed region of
+        # the headline value.
+        pl = measure_pipeline("llama3-8b-w8a8", world, rank, local, dev, steps=128)
+        if rank == 0:
+            pl["note"] = ("layer-range pipeline over the ranks (batch 1: stages run one after "
+                          "another); timed separately from the headline value")
+            line["pipeline"] = pl
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -517,41 +529,69 @@ def model_bytes_per_token(shape, q8, ctx):
     return L * layer_w + cls + kv_bytes
 
 
-def run_model(args):
-    """Prefill a random prompt, then greedy-decode, through N pipeline stages
-    (N = the number of ranks; 1 = the single-GPU engine).  Synthetic
-    N(0, 0.02) weights (W8A8: quantized per group of 64) generated on the
-    device; RMSNorm weights 1.0.  Decode tok/s is timed from the first
-    generated token, as the reference's generate() does (main.cpp:100-107)."""
+def hop_latency(comm, rank, dim, dev, iters=200):
+    """One stage hop of the pipeline, measured: a ping-pong of one
+    activation row x[dim] FP32 between ranks 0 and 1 through the stage
+    transport, timed with CUDA events on rank 0's stream.  Returns the
+    one-way time in microseconds on rank 0 (None elsewhere); ranks other
+    than 0 and 1 take no part."""
+    import torch
+    if rank > 1:
+        return None
+    x = torch.zeros(dim, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def rounds(n):
+        for _ in range(n):
+            if rank == 0:
+                comm.send(x, 1)
+                comm.recv(x, 1)
+            else:
+                comm.recv(x, 0)
+                comm.send(x, 0)
+
+    rounds(20)
+    torch.cuda.synchronize(dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    rounds(iters)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    return e0.elapsed_time(e1) * 1e3 / iters / 2 if rank == 0 else None
+
+
+def measure_pipeline(model, world, rank, local, dev, prompt_len=None, steps=None, warm=3,
+                     comm_kind="native", q8_gemv=None, want_e2e=False):
+    """Prefill a random prompt, then greedy-decode, through `world` layer-range
+    pipeline stages (1 = the single-GPU engine), on an already initialised
+    process group.  Synthetic N(0, 0.02) weights (W8A8: quantized per group
+    of 64) generated on the device; RMSNorm weights 1.0.  Decode tok/s is
+    timed from the first generated token, as the reference's generate() does
+    (main.cpp:100-107); times are CUDA events, max over ranks.
+
+    Returns a dict on rank 0 (None elsewhere): decode tok/s, prefill seconds,
+    each stage's layer compute per token, and the measured hop time."""
     import torch
     import torch.distributed as dist
     from leap_b200 import ModelConfig, Transformer
     from leap_b200.pipeline import PipelineStage, stage_range
 
-    shape, q8, theta, prompt_len, gen = MODELS[args.model]
-    prompt_len = args.prompt or prompt_len
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        import datetime
-        os.environ.setdefault("TORCH_NCCL_SHOW_EAGER_INIT_P2P_SERIALIZATION_WARNING", "false")
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    shape, q8, theta, p_len, gen = MODELS[model]
+    prompt_len = prompt_len or p_len
     cfg = ModelConfig(*shape)
     lb, le = stage_range(cfg.n_layers, rank, world)
     chunk = 512
-    if args.q8_gemv is not None:
+    if q8_gemv is not None:
         from leap_b200._native import check as _check, lib as _lib
-        _check(_lib().leap_op_set_q8_gemv(args.q8_gemv))
+        _check(_lib().leap_op_set_q8_gemv(q8_gemv))
     eng = Transformer.synthetic(cfg, q8, seed=SEED, device=local, rope_theta=theta,
                                 layer_range=(lb, le), max_chunk=chunk)
     eng.bind_torch_stream()
     comm = None
     if world > 1:
         from leap_b200.pipeline import NativeComm, TorchComm
-        comm = NativeComm(rank, world, local) if args.comm == "native" else TorchComm()
+        comm = NativeComm(rank, world, local) if comm_kind == "native" else TorchComm()
     stage = PipelineStage(eng, cfg.dim, dev, max_chunk=chunk, rank=rank, world=world, comm=comm)
     prompt = [int(t) for t in np.random.default_rng(SEED).integers(0, cfg.vocab_size,
                                                                      prompt_len)]
@@ -568,6 +608,14 @@ def run_model(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    def sum_over_ranks(x):
+        if world == 1:
+            return [x]
+        t = torch.zeros(world, device=dev, dtype=torch.float64)
+        t[rank] = x
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        return [float(v) for v in t.tolist()]
+
     def timed(fn):
         barrier()
         torch.cuda.synchronize(dev)
@@ -582,29 +630,36 @@ def run_model(args):
 
     # warm-up: a short prompt and a few tokens, then a clean cache
     stage.prefill(prompt[:64], 0)
-    stage.decode(64, args.warmup)
+    stage.decode(64, warm)
     torch.cuda.synchronize(dev)
     eng.clear_kv_cache()
 
-    sampler = ClockSampler(local)
-    sampler.start()
     _, prefill_s = timed(lambda: stage.prefill(prompt, 0))
-    warm = args.warmup
-    steps = args.steps if args.steps_given else gen - 1 - warm
+    steps = steps or gen - 1 - warm
     stage.decode(prompt_len, warm)  # untimed decode steps, positions continue
     toks, decode_s = timed(lambda: stage.decode(prompt_len + warm, steps))
-    clocks = sampler.stop()
     ctx_mid = prompt_len + warm + steps // 2
-    per_tok = model_bytes_per_token(shape, q8, ctx_mid)
-    tok_s = steps / decode_s
-    peak, peak_kind = load_peaks()
+
+    # each stage's own layer compute per decode token (no hand-off): the
+    # same rows again, with this stage's layers alone
+    x1 = torch.randn((1, cfg.dim), device=dev)
+    barrier()
+    torch.cuda.synchronize(dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    n_c = min(steps, 64)
+    e0.record(stream)
+    for i in range(n_c):
+        eng.layers(prompt_len + warm + i, x1)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    stage_compute_us = sum_over_ranks(e0.elapsed_time(e1) * 1e3 / n_c)
+    hop_us = hop_latency(comm, rank, cfg.dim, dev) if world > 1 else None
 
     e2e = None
-    if world == 1 and not args.no_e2e:
+    if world == 1 and want_e2e:
         # the reference-facing call: forward(token, pos) with the logits read
         # back to the host every step (Transformer.h:56)
-        # positions re-used from the timed run (rows are rewritten; the
-        # attention work per token is the same)
         nxt = int(toks[-1].item())
         n_e2e = min(steps, 64)
         pos = prompt_len + warm + steps - n_e2e
@@ -616,50 +671,96 @@ def run_model(args):
         e2e = {"value": round(n_e2e / e2e_s, 2), "unit": "tok/s",
                "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4 * cfg.vocab_size + 4,
                "path": "Transformer.forward(token, pos) -> host logits, per token"}
+    eng.close()
+    if comm is not None:
+        torch.cuda.synchronize(dev)
+        comm.close()
+    barrier()
+    if rank != 0:
+        return None
+    step_us = decode_s / steps * 1e6
+    # per token: embedding; per layer 12 kernels (W8A8: norm, quantize, qkv,
+    # attention, quantize, wo, norm, quantize, w13, silu, quantize, w2) or 8
+    # (FP32); head: norm, [quantize], classifier, argmax
+    n_launch = 1 + 12 * cfg.n_layers + 4 if q8 else 1 + 8 * cfg.n_layers + 3
+    return {"model": model, "stages": [list(stage_range(cfg.n_layers, r, world))
+                                       for r in range(world)],
+            "decode_tok_s": round(steps / decode_s, 2), "decode_steps": steps,
+            "decode_us_per_token": round(step_us, 2),
+            "prefill_tokens": prompt_len, "prefill_s": round(prefill_s, 3),
+            "prefill_tok_s": round(prompt_len / prefill_s, 1),
+            "stage_compute_us_per_token": [round(v, 2) for v in stage_compute_us],
+            "hand_off_us_per_token": round(step_us - sum(stage_compute_us), 2),
+            "hops_per_token": world if world > 1 else 0,
+            "hop_us_measured": None if hop_us is None else round(hop_us, 2),
+            "bytes_per_token": int(model_bytes_per_token(shape, q8, ctx_mid)),
+            "ctx_mid": ctx_mid, "q8": q8, "e2e": e2e, "gpu_launches": n_launch * steps,
+            "stage_transport": ("leap_pp (NCCL p2p over NVLink)" if comm_kind == "native"
+                                else "torch.distributed p2p") if world > 1 else None}
 
+
+def run_model(args):
+    """The --model line: measure_pipeline over N ranks (N = 1: the
+    single-GPU engine)."""
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        os.environ.setdefault("TORCH_NCCL_SHOW_EAGER_INIT_P2P_SERIALIZATION_WARNING", "false")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    shape, q8, theta, prompt_len, gen = MODELS[args.model]
+    prompt_len = args.prompt or prompt_len
+    sampler = ClockSampler(local)
+    sampler.start()
+    pl = measure_pipeline(args.model, world, rank, local, dev, prompt_len=prompt_len,
+                          steps=args.steps if args.steps_given else None, warm=args.warmup,
+                          comm_kind=args.comm, q8_gemv=args.q8_gemv,
+                          want_e2e=not args.no_e2e)
+    clocks = sampler.stop()
     line = None
     if rank == 0:
-        # per token: embedding; per layer 12 kernels (W8A8: norm, quantize,
-        # qkv, attention, quantize, wo, norm, quantize, w13, silu, quantize, w2)
-        # or 8 (FP32); head: norm, [quantize], classifier, argmax
-        n_layers_launch = 1 + 12 * cfg.n_layers + 4 if q8 else 1 + 8 * cfg.n_layers + 3
+        tok_s = pl["decode_tok_s"]
+        per_tok = pl["bytes_per_token"]
+        peak, peak_kind = load_peaks()
         line = {
-            "metric": f"decode tok/s ({args.model})", "value": round(tok_s, 2), "unit": "tok/s",
-            "n_gpus": world, "steps": steps, "warmup": warm,
-            "ms_per_step": round(decode_s / steps * 1e3, 4), "higher_is_better": True,
+            "metric": f"decode tok/s ({args.model})", "value": tok_s, "unit": "tok/s",
+            "n_gpus": world, "steps": pl["decode_steps"], "warmup": args.warmup,
+            "ms_per_step": round(pl["decode_us_per_token"] / 1e3, 4), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "int8 x int8 -> f32" if q8
             else "f32", "data": "synthetic (seeded N(0,0.02) weights on device, random ids)",
             "config": {"workload": f"{args.model}: batch 1, {prompt_len}-token prompt prefilled, "
                                    f"then greedy decode", "model": args.model,
-                       "global_batch": 1, "seq_len": prompt_len + warm + steps,
+                       "global_batch": 1, "seq_len": prompt_len + args.warmup + pl["decode_steps"],
                        "parallelism": f"pp{world}" if world > 1 else "single",
-                       "stage_transport": (("leap_pp (NCCL p2p)" if args.comm == "native"
-                                            else "torch.distributed p2p") if world > 1
-                                           else None),
-                       "stages": [list(stage_range(cfg.n_layers, r, world))
-                                  for r in range(world)],
+                       "stage_transport": pl["stage_transport"], "stages": pl["stages"],
                        "l2": f"inputs > L2: {per_tok / 1e9:.2f} GB of weights and KV per token"},
-            "prefill": {"tokens": prompt_len, "seconds": round(prefill_s, 3),
-                        "tok_s": round(prompt_len / prefill_s, 1)},
+            "prefill": {"tokens": prompt_len, "seconds": pl["prefill_s"],
+                        "tok_s": pl["prefill_tok_s"]},
+            "pipeline": {k: pl[k] for k in ("stage_compute_us_per_token", "hand_off_us_per_token",
+                                            "hops_per_token", "hop_us_measured")},
             "roofline": {"bound": "hbm", "achieved": round(per_tok * tok_s / 1e9, 1),
                          "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
                          "frac": round(per_tok * tok_s / 1e9 / peak, 4),
                          "bytes_per_token": int(per_tok), "traffic": None,
                          "note": "whole decode step (all kernels) against one GPU's HBM; "
                                  "stages run one after another for batch 1"},
-            "e2e": e2e,
-            "gpu_launches": n_layers_launch * steps,
+            "e2e": pl["e2e"],
+            "gpu_launches": pl["gpu_launches"],
             "clocks": clocks,
         }
-    eng.close()
     if world > 1:
         torch.cuda.synchronize(dev)
-        comm.close()
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = model_cpu_baseline(args.model, prompt_len + warm + steps // 2,
-                                                  args.cpu_seconds)
+        line["cpu_baseline"] = model_cpu_baseline(args.model, prompt_len + args.warmup
+                                                  + pl["decode_steps"] // 2, args.cpu_seconds)
     if rank == 0:
         emit(line)
 
@@ -838,6 +939,8 @@ def main():
                          "2 persistent bulk-copy (default: the library's, 2)")
     ap.add_argument("--comm", choices=["native", "torch"], default="native",
                     help="stage transport for --model on N > 1 ranks")
+    ap.add_argument("--no-pipeline", action="store_true",
+                    help="skip the 8B W8A8 layer-range pipeline of the default line")
     args = ap.parse_args()
     _keep_stdout_for_result()
     args.steps_given = args.steps is not None

@@ -32,6 +32,8 @@ PORT_SO = os.path.join(HERE, "_build", "liboracle.so")
 REF_ATTN_SO = os.path.join(HERE, "_ref", "libleapref_attn.so")
 REF_ENGINE_SO = os.path.join(HERE, "_ref", "libleapref_engine.so")
 REF_ENGINE_10K_SO = os.path.join(HERE, "_ref", "libleapref_engine_10k.so")
+# the reference engine with its attention block calling libleap_b200.so
+REF_ENGINE_GPUATTN_SO = os.path.join(HERE, "_ref", "libleapref_engine_gpuattn.so")
 
 _lock = threading.Lock()
 _libs: dict[str, ctypes.CDLL] = {}
@@ -74,6 +76,20 @@ def build_ref() -> bool:
         return False
     subprocess.run(["make", "-s", "-C", HERE, "ref", f"REF={ref}"], check=True)
     return True
+
+
+def build_binding() -> bool:
+    """Compile the reference engine bound to the C ABI (needs the reference
+    sources and the built libleap_b200.so)."""
+    ref = reference_root()
+    if ref is None:
+        return False
+    subprocess.run(["make", "-s", "-C", HERE, "binding", f"REF={ref}"], check=True)
+    return True
+
+
+def has_ref_binding() -> bool:
+    return os.path.exists(REF_ENGINE_GPUATTN_SO)
 
 
 def _load(path: str) -> ctypes.CDLL:
@@ -229,10 +245,16 @@ class RefEngine:
     """The reference engine on a .bin file: forward(token, pos) -> logits.
 
     theta_10k selects the copy built with the RoPE literal set to 10000
-    (TinyLlama); the shipped reference hard-codes 500000."""
+    (TinyLlama); the shipped reference hard-codes 500000.  gpu_attention
+    selects the reference engine built with its attention block bound to
+    libleap_b200.so (oracle/ref_binding_attn.cpp; theta 500000)."""
 
-    def __init__(self, path: str, theta_10k: bool = False):
-        so = REF_ENGINE_10K_SO if theta_10k else REF_ENGINE_SO
+    def __init__(self, path: str, theta_10k: bool = False, gpu_attention: bool = False):
+        if gpu_attention:
+            # the reference engine whose attention block calls libleap_b200.so
+            so = REF_ENGINE_GPUATTN_SO
+        else:
+            so = REF_ENGINE_10K_SO if theta_10k else REF_ENGINE_SO
         if not os.path.exists(so):
             raise FileNotFoundError(f"{so} missing: run `make -C oracle ref`")
         lib = _load(so)
