@@ -1,6 +1,6 @@
 // common.cuh — shared device helpers for the sm_100a kernels.
 //
-// mbarrier + bulk-copy (TMA, non-tensor, no multicast) primitives written as
+// mbarrier + bulk-copy (TMA, non-tensor, this CTA's shared memory only) primitives written as
 // inline PTX, bounded waits that report through an error word instead of
 // trapping, and small math helpers.
 #pragma once
@@ -132,7 +132,7 @@ __device__ __forceinline__ bool mbar_test(uint64_t *bar, uint32_t parity) {
 
 // One-dimensional bulk copy global -> shared (TMA engine), completing
 // `bytes` of transaction count on `bar`.  src/dst 16-byte aligned, bytes a
-// multiple of 16.  No cluster multicast.
+// multiple of 16.  The destination is this CTA's own shared memory.
 __device__ __forceinline__ void bulk_g2s(void *dst_smem, const void *src_gmem,
                                          uint32_t bytes, uint64_t *bar) {
     asm volatile(

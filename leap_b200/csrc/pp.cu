@@ -109,8 +109,13 @@ int settle(leap_pp *pp, ncclResult_t first, const char *what) {
         leap::set_error("%s: %s", what, api.GetErrorString(first));
         return LEAP_ERR_COMM;
     }
-    const auto deadline = clk::now() + std::chrono::milliseconds(pp->timeout_ms);
-    for (;;) {
+    // An enqueue on a non-blocking communicator usually settles within
+    // microseconds: poll without sleeping at first (a sleep here delays the
+    // stage's next launches and shows up as hop latency), then yield, then
+    // back off to short sleeps; all bounded by the deadline.
+    const auto start = clk::now();
+    const auto deadline = start + std::chrono::milliseconds(pp->timeout_ms);
+    for (unsigned polls = 0;; ++polls) {
         ncclResult_t st = ncclSuccess;
         const ncclResult_t q = api.CommGetAsyncError(pp->comm, &st);
         if (q != ncclSuccess) st = q;
@@ -128,7 +133,11 @@ int settle(leap_pp *pp, ncclResult_t first, const char *what) {
                             pp->timeout_ms);
             return LEAP_ERR_COMM;
         }
-        std::this_thread::sleep_for(std::chrono::microseconds(50));
+        if (polls < 4096) continue;
+        if (clk::now() - start < std::chrono::milliseconds(2))
+            std::this_thread::yield();
+        else
+            std::this_thread::sleep_for(std::chrono::microseconds(20));
     }
 }
 
