@@ -88,8 +88,10 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_tc_pipe_kernel(const PAr
     unsigned char *base = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
     const uint32_t sbase = smem_addr(base);
 
-    const int kvh = blockIdx.y;
-    const int t0 = (gridDim.x - 1 - blockIdx.x) * BT;  // longest rows first
+    // Blocks are dispatched in linear order (x fastest): x = kv head, y = the
+    // query block counted from the end, so the whole grid runs longest-first.
+    const int kvh = blockIdx.x;
+    const int t0 = (gridDim.y - 1 - blockIdx.y) * BT;
     const int t_last = min(t0 + BT, a.n_tok) - 1;
     const int kv_end = a.pos0 + t_last + 1;
     const int n_kt = (kv_end + kPKeys - 1) / kPKeys;
@@ -425,7 +427,7 @@ int launch_pipe_g(leap_ctx *c, const PArgs &a) {
     const void *fn = reinterpret_cast<const void *>(prefill_tc_pipe_kernel<G>);
     if (const int st = set_kernel_smem(fn, kPSmem, "cudaFuncSetAttribute(prefill_tc_pipe)")) return st;
     constexpr int BT = kPRows / G;
-    dim3 grid((a.n_tok + BT - 1) / BT, c->n_kv);
+    dim3 grid(c->n_kv, (a.n_tok + BT - 1) / BT);
     prefill_tc_pipe_kernel<G><<<grid, kPThreads, kPSmem, c->stream>>>(a);
     return cuda_status(cudaGetLastError(), "prefill_tc_pipe_kernel launch");
 }
