@@ -68,8 +68,9 @@ struct PBars {
     uint64_t q_ready;        // Q hi/lo in TMEM (4 softmax warps)
     uint64_t st_full[2];     // staging b holds tile j (bulk-copy bytes)
     uint64_t st_empty[2];    // converters done with staging b (4 warps)
-    uint64_t op_full[2];     // operand tiles b hold tile j (4 warps)
-    uint64_t op_empty[2];    // PV(j) done: operands b and S/P buffer b free (commit)
+    uint64_t k_full[2];      // K operand tiles b hold tile j (converter warps)
+    uint64_t v_full[2];      // V^T operand tiles b hold tile j (converter warps)
+    uint64_t op_empty[2];    // PV(j) done: V operands b and S/P buffer b free (commit)
     uint64_t s_full[2];      // S(j) done (commit)
     uint64_t p_full[2];      // P(j) in TMEM, O rescaled if needed (4 warps)
 };
@@ -103,7 +104,8 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_tc_pipe_kernel(const PAr
         for (int b = 0; b < 2; ++b) {
             mbar_init(&bars.st_full[b], 1);
             mbar_init(&bars.st_empty[b], kPConv);
-            mbar_init(&bars.op_full[b], kPConv);
+            mbar_init(&bars.k_full[b], kPConv);
+            mbar_init(&bars.v_full[b], kPConv);
             mbar_init(&bars.op_empty[b], 1);
             mbar_init(&bars.s_full[b], 1);
             mbar_init(&bars.p_full[b], 4);
@@ -233,13 +235,15 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_tc_pipe_kernel(const PAr
         }
     } else if (warp < 4 + kPConv) {
         // ================= converter warps: staging -> TF32 hi/lo operands ======
+        // K of tile j goes into buffer j%2 as soon as S(j-2) has read that
+        // buffer's K, so it overlaps PV(j-2); V waits for PV(j-2).
         const int ct = tid - 128;  // 0 .. 32*kPConv-1
         bool ok = true;
         for (int j = 0; j < n_kt && ok; ++j) {
             const int b = j & 1;
             const int nr = min(kPKeys, kv_end - j * kPKeys);
             ok = mbar_wait(&bars.st_full[b], par(j));
-            if (ok && j >= 2) ok = mbar_wait(&bars.op_empty[b], par(j - 2));
+            if (ok && j >= 2) ok = mbar_wait(&bars.s_full[b], par(j - 2));
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) break;
             const float *stK = reinterpret_cast<const float *>(base + kPOffStK(b));
@@ -259,6 +263,11 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_tc_pipe_kernel(const PAr
                 *reinterpret_cast<float4 *>(base + kPOffKhi(b) + off) = h;
                 *reinterpret_cast<float4 *>(base + kPOffKlo(b) + off) = w;
             }
+            fence_proxy_async_smem();  // K operand writes -> visible to the tensor core
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars.k_full[b]);
+            if (j >= 2) ok = __all_sync(0xffffffffu, mbar_wait(&bars.op_empty[b], par(j - 2)));
+            if (!ok) break;
             {
                 // V^T row d, a 1/kVParts share of its keys per thread
                 constexpr int kVParts = 32 * kPConv / kPHd;
@@ -283,11 +292,11 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_tc_pipe_kernel(const PAr
                     *reinterpret_cast<float4 *>(base + kPOffVTlo(b) + off) = w;
                 }
             }
-            fence_proxy_async_smem();  // operand writes -> visible to the tensor core
+            fence_proxy_async_smem();  // V operand writes -> visible to the tensor core
             __syncwarp();
             if (lane == 0) {
                 mbar_arrive(&bars.st_empty[b]);
-                mbar_arrive(&bars.op_full[b]);
+                mbar_arrive(&bars.v_full[b]);
             }
         }
         if (!ok && lane == 0) atomicExch(&s_fail, 1);
@@ -358,10 +367,10 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_tc_pipe_kernel(const PAr
             }
             __syncwarp();
         };
-        // Issue whichever step is ready: S(j) once tile j's operands are
+        // Issue whichever step is ready: S(j) once tile j's K operands are
         // converted and PV(j-2) has released S/P buffer j%2; PV(j) once the
-        // softmax has written P(j); the copy of tile j+2 once the converters
-        // have taken tile j from staging.  Every test is of the next phase of
+        // softmax has written P(j) and tile j's V operands are converted; the
+        // copy of tile j+2 once the converters have taken tile j from staging.  Every test is of the next phase of
         // its barrier only (the one before it was observed), so parities
         // cannot alias.  No progress for kMaxWaitNs ends the loop.
         unsigned long long t_idle = global_ns();
@@ -370,7 +379,7 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_tc_pipe_kernel(const PAr
             bool progress = false;
             if (s_issued < n_kt && s_issued <= pv_issued + 1) {
                 const int j = s_issued, b = j & 1;
-                bool ready = mbar_test(&bars.op_full[b], par(j));
+                bool ready = mbar_test(&bars.k_full[b], par(j));
                 if (ready && j >= 2) ready = mbar_test(&bars.op_empty[b], par(j - 2));
                 if (__all_sync(0xffffffffu, ready)) {
                     tc::fence_after_sync();
@@ -381,7 +390,8 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_tc_pipe_kernel(const PAr
             }
             if (pv_issued < s_issued) {
                 const int j = pv_issued;
-                if (__all_sync(0xffffffffu, mbar_test(&bars.p_full[j & 1], par(j)))) {
+                if (__all_sync(0xffffffffu, mbar_test(&bars.p_full[j & 1], par(j)) &&
+                                                mbar_test(&bars.v_full[j & 1], par(j)))) {
                     tc::fence_after_sync();
                     issue_pv(j);
                     ++pv_issued;

@@ -8,9 +8,10 @@ finish (no deadlock), no wait may target a phase more than one behind the
 barrier (parities would alias), and every buffer is read only after it was
 written for that item and rewritten only after its readers are done.
 
-  prefill_tc_pipe.cu  softmax warps / converter warps / one issuing lane;
-                      the issuer takes whichever of S(j), PV(j), copy(j) is
-                      ready; MMAs complete in issue order.
+  prefill_tc_pipe.cu  softmax warps / converter warps (K and V operands of a
+                      tile in two steps) / one issuing lane; the issuer takes
+                      whichever of S(j), PV(j), copy(j) is ready; MMAs
+                      complete in issue order.
   engine_kernels.cu   gemv_q8_stream_kernel: dot warps / copy producer /
                       chain warp over (row block, chunk) items.
 """
@@ -36,21 +37,27 @@ class Bar:
 
 
 def run_prefill(n_kt, seed, rescale_prob, n_conv=8):
+    """prefill_tc_pipe_kernel.  Converter warps turn staged tile j into K and
+    V operand tiles of buffer j%2 in two steps: K once S(j-2) has read K of
+    that buffer (s_full), V once PV(j-2) has read V (op_empty); k_full and
+    v_full tell the issuer.  S(j) needs K(j) and the S/P TMEM buffer freed by
+    PV(j-2); PV(j) needs P(j) and V(j)."""
     R = random.Random(seed)
     B = {}
     for b in (0, 1):
-        for k, c in (("stf", 1), ("ste", n_conv), ("opf", n_conv), ("ope", 1), ("sf", 1),
-                     ("pf", 4)):
+        for k, c in (("stf", 1), ("ste", n_conv), ("kf", n_conv), ("vf", n_conv), ("ope", 1),
+                     ("sf", 1), ("pf", 4)):
             B[(k, b)] = Bar(c)
-    st = {"stage": {}, "op": {}, "S": {}, "P": {}, "O": 0}
+    st = {"stage": {}, "opK": {}, "opV": {}, "S": {}, "P": {}, "O": 0, "sdone": set(),
+          "pvdone": set()}
     mma, cps = [], []
     sm = [{"j": 0, "ph": 0} for _ in range(4)]
-    cv = [{"j": 0} for _ in range(n_conv)]
+    cv = [{"j": 0, "ph": 0} for _ in range(n_conv)]
     iss = {"ns": 0, "np": 0, "staged": 0}
     for j in range(min(2, n_kt)):
         cps.append(j)
         iss["staged"] += 1
-    for _ in range(200000):
+    for _ in range(300000):
         acts = []
         for w, s in enumerate(sm):
             j = s["j"]
@@ -67,14 +74,18 @@ def run_prefill(n_kt, seed, rescale_prob, n_conv=8):
                     acts.append(("smP", w, resc))
         for w, s in enumerate(cv):
             j = s["j"]
-            if j < n_kt and B[("stf", j & 1)].ready(j >> 1) and \
-                    (j < 2 or B[("ope", j & 1)].ready((j - 2) >> 1)):
-                acts.append(("cv", w))
+            if j >= n_kt:
+                continue
+            if s["ph"] == 0 and B[("stf", j & 1)].ready(j >> 1) and \
+                    (j < 2 or B[("sf", j & 1)].ready((j - 2) >> 1)):
+                acts.append(("cvK", w))
+            elif s["ph"] == 1 and (j < 2 or B[("ope", j & 1)].ready((j - 2) >> 1)):
+                acts.append(("cvV", w))
         ns, np_, sg = iss["ns"], iss["np"], iss["staged"]
-        if ns < n_kt and ns <= np_ + 1 and B[("opf", ns & 1)].ready(ns >> 1) and \
+        if ns < n_kt and ns <= np_ + 1 and B[("kf", ns & 1)].ready(ns >> 1) and \
                 (ns < 2 or B[("ope", ns & 1)].ready((ns - 2) >> 1)):
             acts.append(("S",))
-        if np_ < ns and B[("pf", np_ & 1)].ready(np_ >> 1):
+        if np_ < ns and B[("pf", np_ & 1)].ready(np_ >> 1) and B[("vf", np_ & 1)].ready(np_ >> 1):
             acts.append(("PV",))
         if sg < n_kt and B[("ste", sg & 1)].ready((sg - 2) >> 1):
             acts.append(("stage",))
@@ -102,23 +113,32 @@ def run_prefill(n_kt, seed, rescale_prob, n_conv=8):
         elif a[0] == "smfin":
             assert st["O"] == n_kt
             sm[a[1]]["ph"] = 2
-        elif a[0] == "cv":
+        elif a[0] == "cvK":
             w, j = a[1], cv[a[1]]["j"]
             assert st["stage"].get(j & 1) == j
-            st["op"][(j & 1, w)] = j
+            assert j < 2 or (j - 2) in st["sdone"]  # S(j-2) has read this K buffer
+            st["opK"][(j & 1, w)] = j
+            B[("kf", j & 1)].arrive()
+            cv[w]["ph"] = 1
+        elif a[0] == "cvV":
+            w, j = a[1], cv[a[1]]["j"]
+            assert st["stage"].get(j & 1) == j
+            assert j < 2 or (j - 2) in st["pvdone"]  # PV(j-2) has read this V buffer
+            st["opV"][(j & 1, w)] = j
             B[("ste", j & 1)].arrive()
-            B[("opf", j & 1)].arrive()
+            B[("vf", j & 1)].arrive()
             cv[w]["j"] += 1
+            cv[w]["ph"] = 0
         elif a[0] == "S":
             j = iss["ns"]
-            assert all(st["op"].get((j & 1, w)) == j for w in range(n_conv))
+            assert all(st["opK"].get((j & 1, w)) == j for w in range(n_conv))
             assert all(st["P"].get((j & 1, w)) in (None, j - 2) for w in range(4))
             mma.append(("S", j))
             iss["ns"] += 1
         elif a[0] == "PV":
             j = iss["np"]
             assert all(st["P"].get((j & 1, w)) == j for w in range(4))
-            assert all(st["op"].get((j & 1, w)) == j for w in range(n_conv))
+            assert all(st["opV"].get((j & 1, w)) == j for w in range(n_conv))
             mma.append(("PV", j))
             iss["np"] += 1
         elif a[0] == "stage":
@@ -127,12 +147,17 @@ def run_prefill(n_kt, seed, rescale_prob, n_conv=8):
         elif a[0] == "mma":  # the tensor core completes in issue order
             kind, j = mma.pop(0)
             if kind == "S":
+                # its operands were not rewritten while it was in flight
+                assert all(st["opK"].get((j & 1, w)) == j for w in range(n_conv))
                 for w in range(4):
                     st["S"][(j & 1, w)] = ("S", j)
+                st["sdone"].add(j)
                 B[("sf", j & 1)].arrive()
             else:
+                assert all(st["opV"].get((j & 1, w)) == j for w in range(n_conv))
                 assert st["O"] == j
                 st["O"] = j + 1
+                st["pvdone"].add(j)
                 B[("ope", j & 1)].arrive()
         else:  # a copy lands (copies complete in any order)
             j = cps.pop(R.randrange(len(cps)))
