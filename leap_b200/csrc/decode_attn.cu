@@ -192,15 +192,15 @@ decode_attn_kernel(const DecodeArgs a, const DecodeSeq tab) {
     // stage is full and no copy is in flight until the first stage is
     // released, so that release must come as early as possible.)
 
-    // Wait for tile tt; if it holds row `pos`, rotate k, append k and v to
-    // the cache, and patch the staged tile (the copy may have read the old
-    // row).  False if the wait gave up.
+    // Wait (this thread) for tile tt; if it holds row `pos`, rotate k, append
+    // k and v to the cache, and patch the staged tile (the copy may have read
+    // the old row) — that needs the whole CTA.  False if the wait gave up.
     auto tile_ready = [&](int tt) -> bool {
         bool r = mbar_wait(&full_bar[tt % kStages], (tt / kStages) & 1);
-        r = __syncthreads_and(r);
-        if (!r) return false;
         const int r0 = row_begin + tt * C::TILE;
         if (last_split && pos < r0 + C::TILE) {
+            r = __syncthreads_and(r);
+            if (!r) return false;
             const int rr = pos - r0;
             float *tK = sK + (tt % kStages) * C::TILE * HD;
             float *tV = sV + (tt % kStages) * C::TILE * HD;
@@ -217,7 +217,7 @@ decode_attn_kernel(const DecodeArgs a, const DecodeSeq tab) {
             }
             __syncthreads();
         }
-        return true;
+        return r;
     };
 
     // Scaled scores (log2 units) of this lane group's rows of tile tt;
@@ -313,22 +313,21 @@ decode_attn_kernel(const DecodeArgs a, const DecodeSeq tab) {
         }
     };
 
-    // Every warp is done with tile tt's stage: refill it with tile tt+kStages.
-    auto tile_release = [&](int tt) {
-        __syncthreads();
-        if (tid == 0 && tt + kStages < n_tiles) stage_tile(tt + kStages);
-    };
-
     int failed = -1;  // the tile whose wait gave up
     for (int t = 0; t < n_tiles; ++t) {
-        if (!tile_ready(t)) {
-            failed = t;
-            break;
-        }
+        const bool landed = tile_ready(t);
         float sc[C::RPG][G];
         tile_scores(t, sc);
         tile_accumulate(t, sc);
-        tile_release(t);
+        // One CTA barrier per tile: every warp is done with the stage (refill
+        // it), and a wait that gave up in any thread ends the loop for all
+        // (that tile's values are discarded; its shared reads stayed in
+        // bounds).
+        if (__syncthreads_or(!landed)) {
+            failed = t;
+            break;
+        }
+        if (tid == 0 && t + kStages < n_tiles) stage_tile(t + kStages);
     }
 
     if (failed >= 0) {
