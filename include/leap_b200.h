@@ -378,6 +378,19 @@ LEAP_API int leap_op_qmatmul(void *stream, float *y, const int8_t *xq,
                              const float *xs, const int8_t *wq,
                              const float *ws, int n, int d, int T, int gs,
                              const float *res);
+/* The W8A8 GEMV of a freshly normalised or computed fp32 vector, as the
+ * engine's decode step launches it for wq;wk;wv, wo, w1;w3 and the
+ * classifier (QuantizedTransformer.cpp:680-683, :925-951, :1056-1059):
+ * y = W . q(a) (+ res), a = rmsnorm(x, nw) for nw != NULL (leap_op_rmsnorm)
+ * else a = x, q the 64-group quantization of leap_op_quantize.  The
+ * persistent kernel quantizes (and normalises) in its prologue; results are
+ * bit-identical to leap_op_rmsnorm_quantize / leap_op_quantize followed by
+ * leap_op_qmatmul with T == 1.  x, nw 16-byte aligned; n % 64 == 0; res
+ * may equal y. */
+LEAP_API int leap_op_qmatmul_fused(void *stream, float *y, const float *x,
+                                   const float *nw, const int8_t *wq,
+                                   const float *ws, int n, int d,
+                                   const float *res);
 /* W8A8 GEMV kernel selection for T == 1 (process-wide; tests/benchmarks):
  * 0 = one row per lane with the row's groups sliced over lanes,
  * 1 = register-staged rows with 4-lane group shuffles,

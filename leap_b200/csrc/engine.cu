@@ -462,22 +462,34 @@ int linear_mat(leap_engine *e, float *y, const float *x, const Mat &w, int row0,
 // W8A8: QuantizedTransformer.cpp:654-1012).
 int layers_one(leap_engine *e, int pos, float *x) {
     const leap_model_config &c = e->cfg;
-    const int dim = c.dim, hid = c.hidden_dim, kv = e->kv_dim, gs = c.group_size;
+    const int dim = c.dim, hid = c.hidden_dim, kv = e->kv_dim;
     const bool q8 = c.quantized;
-    // W8A8: the normalised / activated vectors are only consumed quantized,
-    // so RMSNorm and SiLU*up write (q, s) directly (one kernel instead of two)
-    auto norm = [&](const float *w) {
-        return q8 ? rmsnorm_quantize(e->stream, e->aq, e->as, x, w, 1, dim)
-                  : rmsnorm(e->stream, e->xb, x, w, 1, dim);
+    auto norm = [&](const float *w) { return rmsnorm(e->stream, e->xb, x, w, 1, dim); };
+    // W8A8 projections whose input is normalised or freshly computed take it
+    // in fp32 and quantize it in the GEMV's prologue (gemv_q8_fused)
+    auto fused = [&](float *y, const float *in, const float *nw, const Mat &w, int rows,
+                     const float *res) {
+        return gemv_q8_fused(e->stream, y, in, nw, e->aq, e->as, w.q, w.s, w.cols, rows, res,
+                             e->attn->d_err);
     };
     for (int i = 0; i < e->n_local; ++i) {
-        ETRY(norm(e->rms_att + size_t(i) * dim));
-        ETRY(linear_vec(e, e->qkv, e->xb, e->wqkv[i], 0, dim + 2 * kv, nullptr));
+        if (q8) {
+            ETRY(fused(e->qkv, x, e->rms_att + size_t(i) * dim, e->wqkv[i], dim + 2 * kv, nullptr));
+        } else {
+            ETRY(norm(e->rms_att + size_t(i) * dim));
+            ETRY(linear_vec(e, e->qkv, e->xb, e->wqkv[i], 0, dim + 2 * kv, nullptr));
+        }
         ETRY(leap_attn_decode(e->attn, i, pos, e->qkv, e->qkv + dim, e->qkv + dim + kv, e->att));
-        if (q8) ETRY(quantize(e->stream, e->aq, e->as, e->att, dim, gs));
-        ETRY(linear_vec(e, x, e->att, e->wo[i], 0, dim, x));  // x += wo . att
-        ETRY(norm(e->rms_ffn + size_t(i) * dim));
-        ETRY(linear_vec(e, e->h13, e->xb, e->w13[i], 0, 2 * hid, nullptr));
+        if (q8)
+            ETRY(fused(x, e->att, nullptr, e->wo[i], dim, x));  // x += wo . q(att)
+        else
+            ETRY(linear_vec(e, x, e->att, e->wo[i], 0, dim, x));  // x += wo . att
+        if (q8) {
+            ETRY(fused(e->h13, x, e->rms_ffn + size_t(i) * dim, e->w13[i], 2 * hid, nullptr));
+        } else {
+            ETRY(norm(e->rms_ffn + size_t(i) * dim));
+            ETRY(linear_vec(e, e->h13, e->xb, e->w13[i], 0, 2 * hid, nullptr));
+        }
         if (q8)
             ETRY(silu_mul_quantize(e->stream, e->aq, e->as, e->h13, e->h13 + hid, hid));
         else
@@ -519,12 +531,19 @@ int layers_chunk(leap_engine *e, int pos0, int T, float *x) {
 
 int head(leap_engine *e, float *x, float *logits, int *token) {
     const leap_model_config &c = e->cfg;
-    if (c.quantized)  // x is only consumed quantized (QuantizedTransformer.cpp:1056-1059)
-        ETRY(rmsnorm_quantize(e->stream, e->aq, e->as, x, e->rms_final, 1, c.dim));
-    else
-        ETRY(rmsnorm(e->stream, x, x, e->rms_final, 1, c.dim));
     float *lg = logits ? logits : e->logits;
-    ETRY(linear_vec(e, lg, x, e->wcls, 0, c.vocab_size, nullptr));
+    if (c.quantized && !e->wcls.f) {
+        // x is only consumed quantized (QuantizedTransformer.cpp:1056-1059):
+        // norm and quantization in the classifier GEMV's prologue
+        ETRY(gemv_q8_fused(e->stream, lg, x, e->rms_final, e->aq, e->as, e->wcls.q, e->wcls.s,
+                           e->wcls.cols, c.vocab_size, nullptr, e->attn->d_err));
+    } else {
+        if (c.quantized)
+            ETRY(rmsnorm_quantize(e->stream, e->aq, e->as, x, e->rms_final, 1, c.dim));
+        else
+            ETRY(rmsnorm(e->stream, x, x, e->rms_final, 1, c.dim));
+        ETRY(linear_vec(e, lg, x, e->wcls, 0, c.vocab_size, nullptr));
+    }
     if (token)
         ETRY(e->sampler ? leap::sampler_launch(e->sampler, e->stream, lg, token)
                         : argmax(e->stream, token, lg, c.vocab_size));
@@ -835,6 +854,30 @@ int leap_op_qmatmul(void *stream, float *y, const int8_t *xq, const float *xs, c
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
     return T == 1 ? gemv_q8(st, y, xq, xs, wq, ws, n, d, res)
                   : gemm_q8(st, y, xq, xs, wq, ws, n, d, T, res);
+}
+
+int leap_op_qmatmul_fused(void *stream, float *y, const float *x, const float *nw,
+                          const int8_t *wq, const float *ws, int n, int d, const float *res) {
+    leap::clear_error();
+    if (!y || !x || !wq || !ws || n < 64 || n % 64 || d < 1 ||
+        (reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(nw) & 15)) {
+        leap::set_error("qmatmul_fused: bad arguments (n %d, d %d; x, nw 16-byte aligned)", n, d);
+        return LEAP_ERR_INVALID;
+    }
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    // (q, s) of the unfused route, stream-ordered on `st`
+    void *aq = nullptr, *as = nullptr;
+    ETRY(leap::cuda_status(cudaMallocAsync(&aq, size_t(n), st), "cudaMallocAsync(qmatmul_fused)"));
+    if (int rc = leap::cuda_status(cudaMallocAsync(&as, size_t(n / 64) * 4, st),
+                                   "cudaMallocAsync(qmatmul_fused)")) {
+        cudaFreeAsync(aq, st);
+        return rc;
+    }
+    const int rc = gemv_q8_fused(st, y, x, nw, static_cast<int8_t *>(aq), static_cast<float *>(as),
+                                 wq, ws, n, d, res);
+    cudaFreeAsync(aq, st);
+    cudaFreeAsync(as, st);
+    return rc;
 }
 
 int leap_op_set_q8_gemv(int impl) {

@@ -20,6 +20,12 @@ int rmsnorm_quantize(cudaStream_t st, int8_t *q, float *s, const float *x, const
 int quantize(cudaStream_t st, int8_t *q, float *s, const float *x, size_t n, int gs);
 int gemv_q8(cudaStream_t st, float *y, const int8_t *xq, const float *xs, const int8_t *wq,
             const float *ws, int n, int d, const float *res, int *err = nullptr);
+// gemv_q8 of q(rmsnorm(x, nw)) (nw non-null) or q(x): the norm and the
+// quantization in the persistent kernel's prologue where it can, else
+// through (aq, as).  Same bits as the separate kernels.
+int gemv_q8_fused(cudaStream_t st, float *y, const float *x, const float *nw, int8_t *aq,
+                  float *as, const int8_t *wq, const float *ws, int n, int d, const float *res,
+                  int *err = nullptr);
 extern bool g_q8_slice;  // int8 GEMV: sliced one-row-per-lane kernel (else register-staged)
 extern bool g_q8_tma;    // int8 GEMV: persistent bulk-copy kernel (default; takes precedence)
 int gemm_q8(cudaStream_t st, float *y, const int8_t *xq, const float *xs, const int8_t *wq,

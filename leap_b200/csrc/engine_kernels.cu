@@ -351,7 +351,7 @@ gemv_q8_slice_kernel(float *y, const int8_t *__restrict__ xq, const float *__res
 //              quarter-warp touches eight bank groups) into a [row][group]
 //              table (two buffers), then release the stage;
 //   warp 8     issues the copies, each as soon as its stage is released
-//              (the first kPS before griddepcontrol.wait: weights are
+//              (the first kPre before griddepcontrol.wait: weights are
 //              constant);
 //   warp 9     prefetches the next block's weight scales with cp.async and
 //              runs each row's chain
@@ -362,6 +362,7 @@ gemv_q8_slice_kernel(float *y, const int8_t *__restrict__ xq, const float *__res
 constexpr int kPR = 8;                   // rows per block = dot warps
 constexpr int kPK = 2048;                // bytes of a row per item
 constexpr int kPS = 3;                   // stages
+constexpr int kPre = 1;                  // stages requested before griddepcontrol.wait
 constexpr int kPG = kPK / 64;            // groups per item = lanes
 constexpr int kPStage = kPR * kPK;       // bytes per stage
 constexpr int kPThreads = 32 * (kPR + 2);
@@ -370,12 +371,32 @@ __device__ __forceinline__ void cp_async4(void *dst_smem, const void *src) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(dst_smem)), "l"(src)
                  : "memory");
 }
+__device__ __forceinline__ void cp_async16(void *dst_smem, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst_smem)), "l"(src)
+                 : "memory");
+}
 __device__ __forceinline__ void cp_async_wait_all() {
     asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
 }
 
+// The activation comes in one of three forms (PRO):
+//   kProQ8     x already quantized (xq, xs);
+//   kProNorm   fp32 x and a norm weight: the CTA computes rmsnorm_kernel's
+//              normalised row and its 64-groups quantization itself, in
+//              rmsnorm_kernel's operation order (its sum of squares runs as
+//              that kernel's row_threads(n) threads would: thread t sums
+//              float4s t, t + T, ... with fmas, warps reduce by xor
+//              shuffles, then the warp sums), so q/s are bit-identical to
+//              leap_op_rmsnorm_quantize's and the separate kernel goes away;
+//   kProQuant  fp32 x quantized as quantize64_kernel does.
+// The last two take n <= 4096, held in the dot warps' registers.
+constexpr int kProQ8 = 0, kProNorm = 1, kProQuant = 2;
+constexpr int kXV = 4;  // float4s of x per dot-warp thread: n <= 32 * kPR * kXV * 4 = 4096
+
+template <int PRO>
 __global__ void __launch_bounds__(kPThreads)
 gemv_q8_stream_kernel(float *y, const int8_t *__restrict__ xq, const float *__restrict__ xs,
+                      const float *__restrict__ xf, const float *__restrict__ nw,
                       const int8_t *__restrict__ wq, const float *__restrict__ ws, int n, int d,
                       const float *res, int *err) {
     extern __shared__ __align__(128) unsigned char psm[];
@@ -441,16 +462,107 @@ gemv_q8_stream_kernel(float *y, const int8_t *__restrict__ xq, const float *__re
         fence_mbar_init();
     }
     __syncthreads();
+    // Only kPre stages are requested before the dependency wait, the rest
+    // right after it: what is requested after the wait (x) queues behind the
+    // weight bytes still in flight (8B W8A8 decode step: 2.40 ms with one
+    // stage before the wait, 2.44 ms with two).
     if (warp == kPR) {
         Cursor u;
         u.rb = blockIdx.x;
-        for (int it = 0; it < min(kPS, items); ++it, advance(u)) issue(it, u);
+        for (int it = 0; it < min(kPre, items); ++it, advance(u)) issue(it, u);
     }
     if (warp == kPR + 1) fetch_scales(0);
-    pdl_enter();
-    for (int i = tid; i < (n >> 4); i += blockDim.x) sx[i] = reinterpret_cast<const int4 *>(xq)[i];
-    for (int g = tid; g < ng; g += blockDim.x) sxs[g] = xs[g];
-    __syncthreads();
+    auto issue_rest = [&]() {  // producer warp: stages kPre .. kPS-1
+        Cursor u;
+        u.rb = blockIdx.x;
+        for (int it = 0; it < min(kPre, items); ++it) advance(u);
+        for (int it = kPre; it < min(kPS, items); ++it, advance(u)) issue(it, u);
+    };
+    if (PRO != kProQ8) {
+        // x (and the norm weight) in registers: dot-warp thread (warp, lane)
+        // holds float4s (warp + 8 k) * 32 + lane, k < kXV, i.e. for k it is
+        // lane `lane` of rmsnorm_kernel's warp warp + 8 k (n <= 4096: that
+        // kernel's threads then hold one float4 each)
+        const int n4 = n >> 2;
+        const float4 *x4 = reinterpret_cast<const float4 *>(xf);
+        float4 xv[kXV], wv[kXV];
+        if (PRO == kProNorm && warp < kPR) {  // the norm weight is constant
+#pragma unroll
+            for (int k = 0; k < kXV; ++k) {
+                const int i = (warp + kPR * k) * 32 + lane;
+                wv[k] = i < n4 ? reinterpret_cast<const float4 *>(nw)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        }
+        pdl_enter();
+        __shared__ float red[32];
+        if (warp == kPR) {
+            issue_rest();
+        } else if (warp < kPR) {
+#pragma unroll
+            for (int k = 0; k < kXV; ++k) {
+                const int i = (warp + kPR * k) * 32 + lane;
+                xv[k] = i < n4 ? x4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+            if (PRO == kProNorm) {
+                // rmsnorm_kernel's per-thread fma chain and warp reduction
+#pragma unroll
+                for (int k = 0; k < kXV; ++k) {
+                    const int vw = warp + kPR * k;
+                    if (vw * 32 >= n4) break;  // warp-uniform
+                    float ss = 0.f;
+                    ss = fmaf(xv[k].x, xv[k].x, ss);
+                    ss = fmaf(xv[k].y, xv[k].y, ss);
+                    ss = fmaf(xv[k].z, xv[k].z, ss);
+                    ss = fmaf(xv[k].w, xv[k].w, ss);
+                    ss = warp_sum(ss);
+                    if (lane == 0) red[vw] = ss;
+                }
+            }
+        }
+        if (PRO == kProNorm) __syncthreads();
+        if (warp < kPR) {
+            float r = 1.f;
+            if (PRO == kProNorm) {
+                // that kernel's second reduction over its n4 / 32 warp sums
+                // (rounded up; every lane ends the xor reduction with the same
+                // value)
+                const int nvw = (n4 + 31) >> 5;
+                const float tot = warp_sum(lane < nvw ? red[lane] : 0.f);
+                float m = tot / float(n);
+                m += 1e-5f;
+                r = 1.0f / sqrtf(m);
+            }
+#pragma unroll
+            for (int k = 0; k < kXV; ++k) {
+                const int i = (warp + kPR * k) * 32 + lane;
+                if ((warp + kPR * k) * 32 >= n4) break;  // whole warps take part in the shuffles
+                const bool valid = i < n4;
+                float4 v = xv[k];
+                if (PRO == kProNorm)
+                    v = make_float4(wv[k].x * (r * v.x), wv[k].y * (r * v.y), wv[k].z * (r * v.z),
+                                    wv[k].w * (r * v.w));
+                quantize16(v, valid, reinterpret_cast<char4 *>(sx), sxs, size_t(i));
+            }
+        }
+        __syncthreads();
+    } else {
+        pdl_enter();
+        if (warp == kPR) {
+            issue_rest();
+        } else if (warp < kPR) {
+            // x and its scales as asynchronous copies, all in flight at once
+            // (a load-then-store loop waits one L2 round trip per
+            // iteration), by the dot warps only: the chain warp's scale
+            // copies, issued before the wait, may still be queued behind
+            // weight bytes and need not have landed here
+            const int nt = kPR * 32;
+            for (int i = tid; i < (n >> 4); i += nt)
+                cp_async16(sx + i, reinterpret_cast<const int4 *>(xq) + i);
+            for (int g = tid; g < ng; g += nt) cp_async4(sxs + g, xs + g);
+            cp_async_wait_all();
+        }
+        __syncthreads();
+    }
 
     if (warp < kPR) {
         // ---- dot warps ------------------------------------------------------
@@ -962,22 +1074,43 @@ size_t gemv_q8_stream_smem(int n) {
     return size_t(kPS) * kPStage + size_t(n) + size_t(n / 64) * 4 * (1 + 2 * kPR);
 }
 
-int gemv_q8_stream(cudaStream_t st, float *y, const int8_t *xq, const float *xs,
-                   const int8_t *wq, const float *ws, int n, int d, const float *res, int *err) {
+template <int PRO>
+int gemv_q8_stream(cudaStream_t st, float *y, const int8_t *xq, const float *xs, const float *xf,
+                   const float *nw, const int8_t *wq, const float *ws, int n, int d,
+                   const float *res, int *err) {
     const size_t smem = gemv_q8_stream_smem(n);
-    const int r = set_kernel_smem(reinterpret_cast<const void *>(gemv_q8_stream_kernel),
+    const int r = set_kernel_smem(reinterpret_cast<const void *>(gemv_q8_stream_kernel<PRO>),
                                   kGemvSmemMax, "cudaFuncSetAttribute(gemv_q8_stream)");
     if (r != LEAP_OK) return r;
     int dev = 0, sms = 0, per_sm = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-        &per_sm, gemv_q8_stream_kernel, kPThreads, smem);
+        &per_sm, gemv_q8_stream_kernel<PRO>, kPThreads, smem);
     if (e != cudaSuccess) return cuda_status(e, "gemv_q8_stream occupancy");
     const int nblocks = (d + kPR - 1) / kPR;
     const int grid = std::max(1, std::min(nblocks, sms * std::max(per_sm, 1)));
-    return launch_pdl("gemv_q8_stream", gemv_q8_stream_kernel, dim3(unsigned(grid)),
-                      dim3(kPThreads), smem, st, y, xq, xs, wq, ws, n, d, res, err);
+    return launch_pdl("gemv_q8_stream", gemv_q8_stream_kernel<PRO>, dim3(unsigned(grid)),
+                      dim3(kPThreads), smem, st, y, xq, xs, xf, nw, wq, ws, n, d, res, err);
+}
+
+// y = W . q(a) (+ res) where a is rmsnorm(x, nw) (pro 1, nw non-null) or x
+// itself (pro 2), q the 64-group activation quantization: the quantization
+// (and norm) run in the GEMV's prologue when the persistent kernel is
+// selected and n <= 4096; otherwise rmsnorm_quantize /
+// quantize write (aq, as) and gemv_q8 follows.  Same bits either way.
+int gemv_q8_fused(cudaStream_t st, float *y, const float *x, const float *nw, int8_t *aq,
+                  float *as, const int8_t *wq, const float *ws, int n, int d, const float *res,
+                  int *err) {
+    const bool aligned = (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+                         (reinterpret_cast<uintptr_t>(nw) & 15) == 0;
+    if (g_q8_tma && n % 64 == 0 && aligned && n <= 32 * kPR * kXV * 4)
+        return nw ? gemv_q8_stream<kProNorm>(st, y, nullptr, nullptr, x, nw, wq, ws, n, d, res, err)
+                  : gemv_q8_stream<kProQuant>(st, y, nullptr, nullptr, x, nullptr, wq, ws, n, d,
+                                              res, err);
+    if (int rc = nw ? rmsnorm_quantize(st, aq, as, x, nw, 1, n) : quantize(st, aq, as, x, n, 64))
+        return rc;
+    return gemv_q8(st, y, aq, as, wq, ws, n, d, res, err);
 }
 
 int gemv_q8_slice(cudaStream_t st, float *y, const int8_t *xq, const float *xs, const int8_t *wq,
@@ -1001,7 +1134,7 @@ int gemv_q8(cudaStream_t st, float *y, const int8_t *xq, const float *xs, const 
     // that the tiled kernel (same accumulation order) takes over
     if (smem > kGemvSmemMax) return gemm_q8(st, y, xq, xs, wq, ws, n, d, 1, res);
     if (g_q8_tma && gemv_q8_stream_smem(n) <= kGemvSmemMax)
-        return gemv_q8_stream(st, y, xq, xs, wq, ws, n, d, res, err);
+        return gemv_q8_stream<kProQ8>(st, y, xq, xs, nullptr, nullptr, wq, ws, n, d, res, err);
     if (g_q8_slice) return gemv_q8_slice(st, y, xq, xs, wq, ws, n, d, res, smem);
     const int r = set_kernel_smem(reinterpret_cast<const void *>(gemv_q8_kernel), kGemvSmemMax,
                                 "cudaFuncSetAttribute(gemv_q8)");

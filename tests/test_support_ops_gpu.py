@@ -69,7 +69,7 @@ def q8_gemv(request):
 
 @pytest.mark.parametrize("n,d", [(2048, 256), (4096, 6144), (14336, 4096), (8192, 1024),
                                  (28672, 256), (65536, 64), (5632, 37), (4096, 3), (256, 9),
-                                 (4160, 100)])
+                                 (4160, 100), (4160, 4001), (6208, 3601)])
 def test_qmatmul_gemv_bit_exact(cuda, q8_gemv, n, d):
     r = np.random.default_rng(n * 7 + d)
     x = r.standard_normal(n).astype(np.float32)
@@ -88,6 +88,46 @@ def test_qmatmul_gemv_bit_exact(cuda, q8_gemv, n, d):
                                 wq_d.data_ptr(), ws_d.data_ptr(), n, d, 1, 64, res.data_ptr()))
     torch.cuda.synchronize()
     assert np.array_equal(res.cpu().numpy(), (np.arange(d, dtype=np.float32) + ref))
+
+
+@pytest.mark.parametrize("n,d", [(4096, 6144), (4096, 4096), (2048, 300), (320, 77), (64, 9),
+                                 (8192, 1000), (14336, 64)])
+@pytest.mark.parametrize("norm", [True, False], ids=["rmsnorm", "quantize"])
+def test_qmatmul_fused_equals_separate_ops(cuda, n, d, norm):
+    """leap_op_qmatmul_fused (the engine's decode-step GEMV with the norm and
+    quantization in its prologue where x fits the spare stages, else the
+    separate kernels) gives the bits of leap_op_rmsnorm_quantize /
+    leap_op_quantize followed by leap_op_qmatmul, with and without a
+    residual aliasing y; and the oracle's arithmetic for the quantize form."""
+    r = np.random.default_rng(n * 5 + d + norm)
+    x = (r.standard_normal(n) * 3).astype(np.float32)
+    x[:64] = 0  # an all-zero group (scale 0)
+    nw = (1 + 0.1 * r.standard_normal(n)).astype(np.float32)
+    w = (r.standard_normal((d, n)) * 0.02).astype(np.float32)
+    wq, ws = oracle.quantize(w.reshape(-1))
+    x_d, nw_d, wq_d, ws_d = _dev(x), _dev(nw), _dev(wq), _dev(ws)
+    q = torch.empty(n, dtype=torch.int8, device="cuda")
+    sc = torch.empty(n // 64, dtype=torch.float32, device="cuda")
+    if norm:
+        check(lib().leap_op_rmsnorm_quantize(_s(), q.data_ptr(), sc.data_ptr(), x_d.data_ptr(),
+                                             nw_d.data_ptr(), 1, n))
+    else:
+        q, sc = _quantize_dev(x_d)
+    ref = _qmm(q, sc, wq_d, ws_d, n, d, 1)[0]
+    nwp = nw_d.data_ptr() if norm else None
+    y = torch.empty(d, dtype=torch.float32, device="cuda")
+    check(lib().leap_op_qmatmul_fused(_s(), y.data_ptr(), x_d.data_ptr(), nwp, wq_d.data_ptr(),
+                                      ws_d.data_ptr(), n, d, None))
+    res = _dev(np.arange(d, dtype=np.float32))
+    check(lib().leap_op_qmatmul_fused(_s(), res.data_ptr(), x_d.data_ptr(), nwp, wq_d.data_ptr(),
+                                      ws_d.data_ptr(), n, d, res.data_ptr()))
+    torch.cuda.synchronize()
+    assert np.array_equal(y.cpu().numpy(), ref.cpu().numpy())
+    assert np.array_equal(res.cpu().numpy(), np.arange(d, dtype=np.float32) + ref.cpu().numpy())
+    if not norm:
+        xq, xs = oracle.quantize(x)
+        want = oracle.qmatmul(xq, xs, wq.reshape(d, n), ws.reshape(d, n // 64), threads=8)
+        assert np.array_equal(y.cpu().numpy(), want)
 
 
 @pytest.mark.parametrize("T", [2, 33, 100])
