@@ -153,6 +153,13 @@ __device__ __forceinline__ void report_error(int *err, int code) {
     if (err) atomicCAS(err, 0, code);
 }
 
+// report_error, and the code also stored (plainly) to a host-mapped word
+// when the caller waits on the host for this kernel (err_host non-null).
+__device__ __forceinline__ void report_error(int *err, int *err_host, int code) {
+    report_error(err, code);
+    if (err_host) *reinterpret_cast<volatile int *>(err_host) = code;
+}
+
 constexpr float kLog2e = 1.4426950408889634f;
 
 // Interleaved-pair RoPE rotation with separately rounded products, as the

@@ -25,12 +25,13 @@ thread_local char g_err[1024] = {0};
 
 // Select a device for the duration of one ABI call and restore the
 // caller's current device afterwards.
-struct DeviceGuard {
+struct DeviceGuard {  // makes `dev` current; restores the previous device if it differed
     int prev = -1;
     bool ok = false;
     explicit DeviceGuard(int dev) {
         if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
-        ok = (cudaSetDevice(dev) == cudaSuccess);
+        ok = prev == dev || cudaSetDevice(dev) == cudaSuccess;
+        if (prev == dev) prev = -1;
     }
     ~DeviceGuard() {
         if (prev >= 0) cudaSetDevice(prev);
@@ -474,13 +475,17 @@ int leap_attn_decode_host(leap_ctx *c, int layer, int pos, const float *q, const
     DeviceGuard g(c->device);
     const size_t nq = size_t(c->n_heads) * c->hd, nk = size_t(c->n_kv) * c->hd;
     float *hq = c->h_stage, *hk = hq + nq, *hv = hk + nk, *ho = hv + nk;
-    float *dq = c->d_stage, *dk = dq + nq, *dv = dk + nk, *dout = dv + nk;
+    float *dq = c->d_stage, *dk = dq + nq, *dv = dk + nk;
     std::memcpy(hq, q, nq * sizeof(float));
     std::memcpy(hk, k_new, nk * sizeof(float));
     std::memcpy(hv, v_new, nk * sizeof(float));
-    // q|k|v in, decode, out|error word back: three kernels chained by
-    // programmatic dependent launch (stage_host.cu), one synchronization
+    // q|k|v in by a copy kernel reading the mapped pinned buffer
+    // (stage_host.cu), then the decode, chained by programmatic dependent
+    // launch; the decode writes the output, and any error code, straight into
+    // the mapped buffer.  One synchronization.
     float *hq_dev = c->h_stage_dev, *ho_dev = hq_dev + nq + 2 * nk;
+    int *herr = reinterpret_cast<int *>(ho + nq);
+    *reinterpret_cast<volatile int *>(herr) = 0;
     if (int st = leap::launch_stage_in(c->stream, hq_dev, dq, int((nq + 2 * nk) / 4))) return st;
     // the grid before the decode is stage_in, which writes no cache row: the
     // decode may start its K/V copies while it runs
@@ -489,12 +494,12 @@ int leap_attn_decode_host(leap_ctx *c, int layer, int pos, const float *q, const
     tab.n_seq = 1;
     tab.pos[0] = pos;
     tab.slot[0] = 0;
-    if (int st = leap::launch_decode(c, layer, tab, dq, dk, dv, dout)) return st;
-    if (int st = leap::launch_stage_out(c->stream, dout, ho_dev, int((nq + 4) / 4))) return st;
+    c->err_host = reinterpret_cast<int *>(ho_dev + nq);
+    const int st = leap::launch_decode(c, layer, tab, dq, dk, dv, ho_dev);
+    c->err_host = nullptr;
+    if (st) return st;
     LEAP_TRY_CUDA(cudaStreamSynchronize(c->stream), "cudaStreamSynchronize");
-    int err;
-    std::memcpy(&err, ho + nq, sizeof(int));
-    if (err) return leap::check_device_error(c);
+    if (*reinterpret_cast<volatile int *>(herr)) return leap::check_device_error(c);
     std::memcpy(out, ho, nq * sizeof(float));
     return LEAP_OK;
 }

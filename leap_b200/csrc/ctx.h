@@ -51,6 +51,9 @@ struct leap_ctx {
 
     // device error word (kernels report bounded-wait timeouts here)
     int *d_err = nullptr;
+    // set only inside leap_attn_decode_host: the decode kernels also store an
+    // error code to this host-mapped word (the caller waits on the host)
+    int *err_host = nullptr;
 
     // host-pointer entry points: pinned staging and device mirrors
     float *h_stage = nullptr;  // pinned: q | k | v | out for one token
@@ -117,11 +120,9 @@ int plan_decode(const leap_ctx *c, DecodeSeq &tab, int shape);
 
 // decode_cluster.cu: co-resident 16-CTA clusters, and the launch.
 int decode_cluster_capacity(leap_ctx *c, int *n);
-// Host-pointer staging kernels (stage_host.cu): n4 float4s pinned host ->
-// device after everything before on the stream, and device -> pinned host
-// once the previous grid (launched with programmatic serialization) is done.
+// Host-pointer staging kernel (stage_host.cu): n4 float4s pinned host ->
+// device after everything before on the stream.
 int launch_stage_in(cudaStream_t st, const float *h_src, float *d_dst, int n4);
-int launch_stage_out(cudaStream_t st, const float *d_src, float *h_dst, int n4);
 
 int launch_decode_cluster(leap_ctx *c, int layer, const DecodeSeq &tab, const float *q,
                           const float *k_new, const float *v_new, float *out, bool overlap);

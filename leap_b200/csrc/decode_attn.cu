@@ -76,6 +76,7 @@ struct DecodeArgs {
     float *part_ml;      // [parts][MLS]: (M, L) per head, padded to 16 bytes
     unsigned *counters;  // [kMaxSeqPerLaunch][n_kv]
     int *err;
+    int *err_host;       // non-null: error codes also go to this host-mapped word
     int n_kv;
     float scale_log2;    // log2(e) / sqrt(HD)
 };
@@ -335,7 +336,7 @@ decode_attn_kernel(const DecodeArgs a, const DecodeSeq tab) {
         // to land before this CTA's shared memory is released, then report.
         for (int tt = failed + 1; tt < min(failed + kStages, n_tiles); ++tt)
             (void)mbar_wait(&full_bar[tt % kStages], (tt / kStages) & 1);
-        if (tid == 0) report_error(a.err, kDevWaitTimeout);
+        if (tid == 0) report_error(a.err, a.err_host, kDevWaitTimeout);
         return;
     }
 
@@ -444,7 +445,7 @@ decode_attn_kernel(const DecodeArgs a, const DecodeSeq tab) {
     cok = __syncthreads_and(cok);
     if (!cok) {
         (void)mbar_wait(&comb_bar_o, 0);  // let the partials' copy land first
-        if (tid == 0) report_error(a.err, kDevWaitTimeout);
+        if (tid == 0) report_error(a.err, a.err_host, kDevWaitTimeout);
         return;
     }
     // one warp per head: max, rescaled sum, normalised weights
@@ -465,7 +466,7 @@ decode_attn_kernel(const DecodeArgs a, const DecodeSeq tab) {
     cok = mbar_wait(&comb_bar_o, cphase);  // the first chunk of partials
     cok = __syncthreads_and(cok);  // also: every weight is in cW
     if (!cok) {
-        if (tid == 0) report_error(a.err, kDevWaitTimeout);
+        if (tid == 0) report_error(a.err, a.err_host, kDevWaitTimeout);
         return;
     }
     cphase ^= 1u;
@@ -485,7 +486,7 @@ decode_attn_kernel(const DecodeArgs a, const DecodeSeq tab) {
             cok = mbar_wait(&comb_bar_o, cphase);
             cok = __syncthreads_and(cok);
             if (!cok) {
-                if (tid == 0) report_error(a.err, kDevWaitTimeout);
+                if (tid == 0) report_error(a.err, a.err_host, kDevWaitTimeout);
                 return;
             }
             cphase ^= 1u;
@@ -760,6 +761,7 @@ int launch_decode(leap_ctx *c, int layer, const DecodeSeq &seqs, const float *q,
     a.part_ml = c->part_ml[c->parity];
     a.counters = c->counters[c->parity];
     a.err = c->d_err;
+    a.err_host = c->err_host;
     a.n_kv = c->n_kv;
     a.scale_log2 = kLog2e / sqrtf(float(c->hd));
     const int st = shape == 0 ? launch_width<0>(c, a, tab, total, overlap, tail)

@@ -53,6 +53,7 @@ struct ClusterArgs {
     const float *rope_cos, *rope_sin;
     size_t head_stride, layer_off, slot_stride;
     int *err;
+    int *err_host;  // non-null: error codes also go to this host-mapped word
     int n_kv;
     float scale_log2;
 };
@@ -249,7 +250,7 @@ decode_cluster_kernel(const ClusterArgs a, const DecodeSeq tab) {
         // and contribute an empty partial so the cluster still completes.
         for (int tt = t + 1; tt < min(t + kCStages, n_tiles); ++tt)
             (void)mbar_wait(&full_bar[tt % kCStages], (tt / kCStages) & 1);
-        if (tid == 0) report_error(a.err, kDevWaitTimeout);
+        if (tid == 0) report_error(a.err, a.err_host, kDevWaitTimeout);
 #pragma unroll
         for (int g = 0; g < G; ++g) {
             m[g] = -INFINITY;
@@ -441,6 +442,7 @@ int launch_decode_cluster(leap_ctx *c, int layer, const DecodeSeq &tab, const fl
     a.layer_off = size_t(layer) * c->layer_stride;
     a.slot_stride = c->slot_stride;
     a.err = c->d_err;
+    a.err_host = c->err_host;
     a.n_kv = c->n_kv;
     a.scale_log2 = kLog2e / sqrtf(float(c->hd));
     switch (c->hd * 100 + c->group) {
