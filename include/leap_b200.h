@@ -378,6 +378,15 @@ LEAP_API int leap_op_qmatmul(void *stream, float *y, const int8_t *xq,
                              const float *xs, const int8_t *wq,
                              const float *ws, int n, int d, int T, int gs,
                              const float *res);
+/* The FP32 GEMV of a normalised vector, as the engine's decode step
+ * launches it for wq;wk;wv and w1;w3 (FloatTransformer.cpp:397-402,
+ * :663-669): y = W . rmsnorm(x, nw) (+ res) (nw != NULL; NULL: y = W . x +
+ * res), the norm formed in the GEMV's prologue with leap_op_rmsnorm's
+ * operation order: bit-identical to leap_op_rmsnorm followed by
+ * leap_op_matmul with T == 1.  n % 4 == 0; res may equal y. */
+LEAP_API int leap_op_matmul_fused(void *stream, float *y, const float *x,
+                                  const float *nw, const float *w, int n,
+                                  int d, const float *res);
 /* The W8A8 GEMV of a freshly normalised or computed fp32 vector, as the
  * engine's decode step launches it for wq;wk;wv, wo, w1;w3 and the
  * classifier (QuantizedTransformer.cpp:680-683, :925-951, :1056-1059):

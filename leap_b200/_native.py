@@ -106,6 +106,8 @@ SIGNATURES: dict[str, tuple] = {
                                c_void_p]),
     "leap_op_qmatmul": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                 c_int, c_int, c_int, c_int, c_void_p]),
+    "leap_op_matmul_fused": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int,
+                                     c_int, c_void_p]),
     "leap_op_qmatmul_fused": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                       c_int, c_int, c_void_p]),
     "leap_op_argmax": (c_int, [c_void_p, c_void_p, c_void_p, c_int]),

@@ -464,9 +464,13 @@ int layers_one(leap_engine *e, int pos, float *x) {
     const leap_model_config &c = e->cfg;
     const int dim = c.dim, hid = c.hidden_dim, kv = e->kv_dim;
     const bool q8 = c.quantized;
-    auto norm = [&](const float *w) { return rmsnorm(e->stream, e->xb, x, w, 1, dim); };
-    // W8A8 projections whose input is normalised or freshly computed take it
-    // in fp32 and quantize it in the GEMV's prologue (gemv_q8_fused)
+    // FP32: the projections of a normalised x form the norm in the GEMV's
+    // prologue (gemv_f32 with the norm weight); W8A8 projections whose input
+    // is normalised or freshly computed take it in fp32 and quantize (and
+    // normalise) it in the GEMV's prologue (gemv_q8_fused)
+    auto norm_vec = [&](float *y, const float *nw, const Mat &w, int rows) {
+        return gemv_f32(e->stream, y, x, w.f, w.cols, rows, nullptr, nw, e->xb);
+    };
     auto fused = [&](float *y, const float *in, const float *nw, const Mat &w, int rows,
                      const float *res) {
         return gemv_q8_fused(e->stream, y, in, nw, e->aq, e->as, w.q, w.s, w.cols, rows, res,
@@ -476,8 +480,7 @@ int layers_one(leap_engine *e, int pos, float *x) {
         if (q8) {
             ETRY(fused(e->qkv, x, e->rms_att + size_t(i) * dim, e->wqkv[i], dim + 2 * kv, nullptr));
         } else {
-            ETRY(norm(e->rms_att + size_t(i) * dim));
-            ETRY(linear_vec(e, e->qkv, e->xb, e->wqkv[i], 0, dim + 2 * kv, nullptr));
+            ETRY(norm_vec(e->qkv, e->rms_att + size_t(i) * dim, e->wqkv[i], dim + 2 * kv));
         }
         ETRY(leap_attn_decode(e->attn, i, pos, e->qkv, e->qkv + dim, e->qkv + dim + kv, e->att));
         if (q8)
@@ -487,8 +490,7 @@ int layers_one(leap_engine *e, int pos, float *x) {
         if (q8) {
             ETRY(fused(e->h13, x, e->rms_ffn + size_t(i) * dim, e->w13[i], 2 * hid, nullptr));
         } else {
-            ETRY(norm(e->rms_ffn + size_t(i) * dim));
-            ETRY(linear_vec(e, e->h13, e->xb, e->w13[i], 0, 2 * hid, nullptr));
+            ETRY(norm_vec(e->h13, e->rms_ffn + size_t(i) * dim, e->w13[i], 2 * hid));
         }
         if (q8)
             ETRY(silu_mul_quantize(e->stream, e->aq, e->as, e->h13, e->h13 + hid, hid));
@@ -854,6 +856,24 @@ int leap_op_qmatmul(void *stream, float *y, const int8_t *xq, const float *xs, c
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
     return T == 1 ? gemv_q8(st, y, xq, xs, wq, ws, n, d, res)
                   : gemm_q8(st, y, xq, xs, wq, ws, n, d, T, res);
+}
+
+int leap_op_matmul_fused(void *stream, float *y, const float *x, const float *nw, const float *w,
+                         int n, int d, const float *res) {
+    leap::clear_error();
+    if (!y || !x || !w || n < 4 || n % 4 || d < 1) {
+        leap::set_error("matmul_fused: bad arguments (n %d, d %d)", n, d);
+        return LEAP_ERR_INVALID;
+    }
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    // the normalised row of the unfused route, stream-ordered on `st`
+    void *xb = nullptr;
+    if (nw)
+        ETRY(leap::cuda_status(cudaMallocAsync(&xb, size_t(n) * 4, st),
+                               "cudaMallocAsync(matmul_fused)"));
+    const int rc = gemv_f32(st, y, x, w, n, d, res, nw, static_cast<float *>(xb));
+    if (xb) cudaFreeAsync(xb, st);
+    return rc;
 }
 
 int leap_op_qmatmul_fused(void *stream, float *y, const float *x, const float *nw,

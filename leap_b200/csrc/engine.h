@@ -30,8 +30,11 @@ extern bool g_q8_slice;  // int8 GEMV: sliced one-row-per-lane kernel (else regi
 extern bool g_q8_tma;    // int8 GEMV: persistent bulk-copy kernel (default; takes precedence)
 int gemm_q8(cudaStream_t st, float *y, const int8_t *xq, const float *xs, const int8_t *wq,
             const float *ws, int n, int d, int T, const float *res);
+// y = W . a (+ res); a = x, or rmsnorm(x, nw) formed in the GEMV's prologue
+// (same bits as rmsnorm followed by the GEMV; xb: a scratch row for the
+// unfused route, used when x is misaligned or too long for shared memory).
 int gemv_f32(cudaStream_t st, float *y, const float *x, const float *w, int n, int d,
-             const float *res);
+             const float *res, const float *nw = nullptr, float *xb = nullptr);
 int gemm_f32(cudaStream_t st, float *y, const float *x, const float *w, int n, int d, int T,
              const float *res);
 int silu_mul(cudaStream_t st, float *h, const float *h3, size_t n);

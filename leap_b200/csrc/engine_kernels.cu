@@ -754,15 +754,21 @@ gemm_q8_kernel(float *y, const int8_t *__restrict__ xq, const float *__restrict_
 
 // ---- FP32 GEMV (FloatTransformer.cpp:240-382) ------------------------------
 // One warp per row (grid-stride), kGemvUnroll float4 weight loads in flight
-// per lane, x in shared memory; y = (res ? res : 0) + W.x.  The first row's
-// first batch of weights is loaded before griddepcontrol.wait.
+// per lane, x in shared memory (asynchronous copies, all in flight at once);
+// y = (res ? res : 0) + W.a.  The first row's first batch of weights is
+// loaded before griddepcontrol.wait.  a = x, or (NORM) rmsnorm_kernel's
+// normalised row w * (r * x), formed in shared memory by this CTA with that
+// kernel's operation order (its sum of squares as its row_threads(n)
+// threads would run it), so the separate RMSNorm launch goes away and the
+// bits stay the same.
+template <bool NORM>
 __global__ void __launch_bounds__(kGemvWarps * 32)
-gemv_f32_kernel(float *y, const float *__restrict__ x, const float *__restrict__ w,
-                int n, int d, const float *res) {
-    extern __shared__ float4 sx4[];
+gemv_f32_kernel(float *y, const float *__restrict__ x, const float *__restrict__ nw,
+                const float *__restrict__ w, int n, int d, const float *res) {
+    extern __shared__ float4 sx4[];  // [n4] x (normalised); NORM: then [n4] norm weight
     const int n4 = n >> 2;
-    const int lane = threadIdx.x & 31;
-    int row = blockIdx.x * kGemvWarps + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int row = blockIdx.x * kGemvWarps + warp;
     float4 a[kGemvUnroll];
     {
         const float4 *wr = reinterpret_cast<const float4 *>(w + size_t(row < d ? row : 0) * n);
@@ -772,14 +778,47 @@ gemv_f32_kernel(float *y, const float *__restrict__ x, const float *__restrict__
             a[u] = (row < d && c < n4) ? ld_stream(wr + c) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
     }
+    if (NORM)  // the norm weight is constant
+        for (int i = threadIdx.x; i < n4; i += blockDim.x)
+            cp_async16(sx4 + n4 + i, reinterpret_cast<const float4 *>(nw) + i);
     pdl_enter();
-    for (int i = threadIdx.x; i < n4; i += blockDim.x) sx4[i] = reinterpret_cast<const float4 *>(x)[i];
+    for (int i = threadIdx.x; i < n4; i += blockDim.x)
+        cp_async16(sx4 + i, reinterpret_cast<const float4 *>(x) + i);
+    cp_async_wait_all();
     __syncthreads();
+    if (NORM) {
+        __shared__ float red[32];
+        const int T = min(1024, max(32, ((n4 + 31) / 32) * 32));  // rmsnorm_kernel's block
+        for (int vw = warp; vw < (T >> 5); vw += kGemvWarps) {
+            float ss = 0.f;
+            for (int i = vw * 32 + lane; i < n4; i += T) {
+                const float4 v = sx4[i];
+                ss = fmaf(v.x, v.x, ss);
+                ss = fmaf(v.y, v.y, ss);
+                ss = fmaf(v.z, v.z, ss);
+                ss = fmaf(v.w, v.w, ss);
+            }
+            ss = warp_sum(ss);
+            if (lane == 0) red[vw] = ss;
+        }
+        __syncthreads();
+        // every lane ends the xor reduction with the same sum
+        const float tot = warp_sum(lane < (T >> 5) ? red[lane] : 0.f);
+        float m = tot / float(n);
+        m += 1e-5f;
+        const float r = 1.0f / sqrtf(m);
+        for (int i = threadIdx.x; i < n4; i += blockDim.x) {
+            const float4 xv = sx4[i], wv = sx4[n4 + i];
+            sx4[i] = make_float4(wv.x * (r * xv.x), wv.y * (r * xv.y), wv.z * (r * xv.z),
+                                 wv.w * (r * xv.w));
+        }
+        __syncthreads();
+    }
     for (; row < d; row += gridDim.x * kGemvWarps) {
         const float4 *wr = reinterpret_cast<const float4 *>(w + size_t(row) * n);
         float acc = 0.f;
         for (int base = 0; base < n4; base += 32 * kGemvUnroll) {
-            if (base > 0 || row != int(blockIdx.x * kGemvWarps + (threadIdx.x >> 5))) {
+            if (base > 0 || row != int(blockIdx.x * kGemvWarps + warp)) {
 #pragma unroll
                 for (int u = 0; u < kGemvUnroll; ++u) {
                     const int c = base + u * 32 + lane;
@@ -1151,19 +1190,37 @@ int gemm_q8(cudaStream_t st, float *y, const int8_t *xq, const float *xs, const 
 }
 
 int gemv_f32(cudaStream_t st, float *y, const float *x, const float *w, int n, int d,
-             const float *res) {
-    const size_t smem = size_t(n) * 4;
+             const float *res, const float *nw, float *xb) {
     if (n % 4 != 0) {
         set_error("gemv_f32: n %d is not a multiple of 4", n);
         return LEAP_ERR_INVALID;
     }
-    if (smem > kGemvSmemMax) return gemm_f32(st, y, x, w, n, d, 1, res);
-    const int r = set_kernel_smem(reinterpret_cast<const void *>(gemv_f32_kernel), kGemvSmemMax,
-                                "cudaFuncSetAttribute(gemv_f32)");
+    const bool aligned = (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+                         (reinterpret_cast<uintptr_t>(nw) & 15) == 0;
+    const size_t smem = size_t(n) * 4 * (nw ? 2 : 1);
+    if (!aligned || smem > kGemvSmemMax) {
+        // unfused: RMSNorm into xb (nw), then the GEMV or the tiled GEMM
+        if (nw) {
+            if (!xb) {
+                set_error("gemv_f32: a normalised input this size needs a scratch row");
+                return LEAP_ERR_INVALID;
+            }
+            if (int rc = rmsnorm(st, xb, x, nw, 1, n)) return rc;
+            x = xb;
+        }
+        if (size_t(n) * 4 > kGemvSmemMax || (reinterpret_cast<uintptr_t>(x) & 15))
+            return gemm_f32(st, y, x, w, n, d, 1, res);
+        return gemv_f32(st, y, x, w, n, d, res);
+    }
+    const void *fn = nw ? reinterpret_cast<const void *>(gemv_f32_kernel<true>)
+                        : reinterpret_cast<const void *>(gemv_f32_kernel<false>);
+    const int r = set_kernel_smem(fn, kGemvSmemMax, "cudaFuncSetAttribute(gemv_f32)");
     if (r != LEAP_OK) return r;
-    const unsigned grid = gemv_grid(reinterpret_cast<const void *>(gemv_f32_kernel), d, smem);
-    return launch_pdl("gemv_f32", gemv_f32_kernel, dim3(grid), dim3(kGemvWarps * 32), smem,
-                      st, y, x, w, n, d, res);
+    const unsigned grid = gemv_grid(fn, d, smem);
+    return nw ? launch_pdl("gemv_f32", gemv_f32_kernel<true>, dim3(grid), dim3(kGemvWarps * 32),
+                           smem, st, y, x, nw, w, n, d, res)
+              : launch_pdl("gemv_f32", gemv_f32_kernel<false>, dim3(grid), dim3(kGemvWarps * 32),
+                           smem, st, y, x, static_cast<const float *>(nullptr), w, n, d, res);
 }
 
 int gemm_f32(cudaStream_t st, float *y, const float *x, const float *w, int n, int d, int T,

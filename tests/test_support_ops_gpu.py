@@ -130,6 +130,34 @@ def test_qmatmul_fused_equals_separate_ops(cuda, n, d, norm):
         assert np.array_equal(y.cpu().numpy(), want)
 
 
+@pytest.mark.parametrize("n,d", [(2048, 2560), (4096, 6144), (320, 77), (64, 9), (5632, 100),
+                                 (28672, 16)])
+def test_matmul_fused_equals_separate_ops(cuda, n, d):
+    """leap_op_matmul_fused (the FP32 decode step's GEMV with the RMSNorm in
+    its prologue where x and the norm weight fit shared memory, else the
+    separate kernels) gives the bits of leap_op_rmsnorm followed by
+    leap_op_matmul, with and without a residual aliasing y."""
+    r = np.random.default_rng(n * 3 + d)
+    x = (r.standard_normal(n) * 3).astype(np.float32)
+    nw = (1 + 0.1 * r.standard_normal(n)).astype(np.float32)
+    w = (r.standard_normal((d, n)) * 0.02).astype(np.float32)
+    x_d, nw_d, w_d = _dev(x), _dev(nw), _dev(w)
+    xb = torch.empty(n, dtype=torch.float32, device="cuda")
+    check(lib().leap_op_rmsnorm(_s(), xb.data_ptr(), x_d.data_ptr(), nw_d.data_ptr(), 1, n))
+    ref = torch.empty(d, dtype=torch.float32, device="cuda")
+    check(lib().leap_op_matmul(_s(), ref.data_ptr(), xb.data_ptr(), w_d.data_ptr(), n, d, 1, None))
+    y = torch.empty(d, dtype=torch.float32, device="cuda")
+    check(lib().leap_op_matmul_fused(_s(), y.data_ptr(), x_d.data_ptr(), nw_d.data_ptr(),
+                                     w_d.data_ptr(), n, d, None))
+    res = _dev(np.arange(d, dtype=np.float32))
+    check(lib().leap_op_matmul_fused(_s(), res.data_ptr(), x_d.data_ptr(), nw_d.data_ptr(),
+                                     w_d.data_ptr(), n, d, res.data_ptr()))
+    torch.cuda.synchronize()
+    assert np.array_equal(y.cpu().numpy(), ref.cpu().numpy())
+    want = (np.arange(d, dtype=np.float32) + ref.cpu().numpy()).astype(np.float32)
+    assert np.array_equal(res.cpu().numpy(), want)
+
+
 @pytest.mark.parametrize("T", [2, 33, 100])
 def test_qmatmul_gemm_equals_gemv_rows(cuda, T):
     n, d = 4096, 1024 + 64
