@@ -679,10 +679,15 @@ def measure_pipeline(model, world, rank, local, dev, prompt_len=None, steps=None
     if rank != 0:
         return None
     step_us = decode_s / steps * 1e6
-    # per token: embedding; per layer 12 kernels (W8A8: norm, quantize, qkv,
-    # attention, quantize, wo, norm, quantize, w13, silu, quantize, w2) or 8
-    # (FP32); head: norm, [quantize], classifier, argmax
-    n_launch = 1 + 12 * cfg.n_layers + 4 if q8 else 1 + 8 * cfg.n_layers + 3
+    # per token: embedding; per layer 6 kernels (qkv with the RMSNorm (and the
+    # quantize) in its prologue, attention, wo (W8A8: quantize prologue), w13
+    # with its RMSNorm, silu(+quantize), w2); W8A8 with dim > 4096 forms the
+    # norm/quantize in separate kernels (3 more); head: classifier (W8A8: with
+    # the final norm in its prologue; FP32: after an RMSNorm launch), argmax
+    fused_q8 = q8 and cfg.dim <= 4096
+    per_layer = 6 + (3 if q8 and not fused_q8 else 0)
+    head = (2 if fused_q8 else 3) if q8 else 3
+    n_launch = 1 + per_layer * cfg.n_layers + head
     return {"model": model, "stages": [list(stage_range(cfg.n_layers, r, world))
                                        for r in range(world)],
             "decode_tok_s": round(steps / decode_s, 2), "decode_steps": steps,
