@@ -180,8 +180,9 @@ LEAP_API int leap_attn_decode(leap_ctx *ctx, int layer, int pos, const float *q,
  * The same call with HOST pointers: the reference-facing form, for an
  * engine whose activations live in host memory like the reference's
  * run_layer.  Copies in, runs, copies out and blocks until `out` is ready
- * (inputs staged through pinned memory that small kernels read and write
- * directly, chained to the decode kernel by programmatic dependent launch).
+ * (inputs staged through pinned memory that a small kernel reads directly,
+ * chained to the decode kernel by programmatic dependent launch; the decode
+ * kernel stores the output into that pinned memory itself).
  */
 LEAP_API int leap_attn_decode_host(leap_ctx *ctx, int layer, int pos, const float *q,
                           const float *k_new, const float *v_new, float *out);
