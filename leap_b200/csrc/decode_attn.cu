@@ -102,7 +102,26 @@ decode_attn_kernel(const DecodeArgs a, const DecodeSeq tab) {
     const int grp = warp * C::RPW + lane / C::LPR;  // row group
 
     // ---- which (sequence, split, kv head) ---------------------------------
-    const int bx = blockIdx.x;
+    // One sequence: blocks are handed out in linear order, and the last few
+    // start only once the previous kernel's combining CTAs leave their SMs
+    // (with no tiles staged before the dependency wait).  So the linear order
+    // is remapped to put every kv head's last split, the short one, at the
+    // end: the late blocks get the least work (14.996 -> 14.85 us per launch
+    // at ctx 8192).  Batches keep (split, kv head) = (x, y).
+    int bx = blockIdx.x;
+    int kvh_sel = blockIdx.y;
+    if (tab.n_seq == 1) {
+        const int T = gridDim.x;
+        const int b = blockIdx.y * T + blockIdx.x;
+        const int n_full = gridDim.y * (T - 1);  // blocks of the non-last splits
+        if (b >= n_full) {
+            bx = T - 1;
+            kvh_sel = b - n_full;
+        } else {
+            bx = b % (T - 1);
+            kvh_sel = b / (T - 1);
+        }
+    }
     int lo = 0, hi = tab.n_seq - 1;
     while (lo < hi) {
         const int mid = (lo + hi + 1) >> 1;
@@ -111,7 +130,7 @@ decode_attn_kernel(const DecodeArgs a, const DecodeSeq tab) {
     const int seq = lo;
     const int split = bx - tab.split0[seq];
     const int nsplit = tab.split0[seq + 1] - tab.split0[seq];
-    const int kvh = blockIdx.y;
+    const int kvh = kvh_sel;
     const int pos = tab.pos[seq];
     const int row_begin = split * tab.chunk;
     const int row_end = min(row_begin + tab.chunk, pos + 1);
