@@ -70,6 +70,7 @@ struct PBars {
     uint64_t st_empty[2];    // converters done with staging b (4 warps)
     uint64_t k_full[2];      // K operand tiles b hold tile j (converter warps)
     uint64_t v_full[2];      // V^T operand tiles b hold tile j (converter warps)
+    uint64_t ph_free[2];     // PV(j)'s P-hi terms done: S columns of buffer b free (commit)
     uint64_t op_empty[2];    // PV(j) done: V operands b and S/P buffer b free (commit)
     uint64_t s_full[2];      // S(j) done (commit)
     uint64_t p_full[2];      // P(j) in TMEM, O rescaled if needed (4 warps)
@@ -106,6 +107,7 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_tc_pipe_kernel(const PAr
             mbar_init(&bars.st_empty[b], kPConv);
             mbar_init(&bars.k_full[b], kPConv);
             mbar_init(&bars.v_full[b], kPConv);
+            mbar_init(&bars.ph_free[b], 1);
             mbar_init(&bars.op_empty[b], 1);
             mbar_init(&bars.s_full[b], 1);
             mbar_init(&bars.p_full[b], 4);
@@ -131,6 +133,13 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_tc_pipe_kernel(const PAr
         const bool row_valid = my_tok < a.n_tok;
         {
             const float *qrow = a.qrot + (size_t(my_tok) * a.n_heads + my_head) * kPHd;
+            // The row's four 128-byte lines are requested into L1 at once, so
+            // only the first chunk below waits a full round trip.
+            if (row_valid) {
+#pragma unroll
+                for (int c = 0; c < kPHd / 32; ++c)
+                    asm volatile("prefetch.global.L1 [%0];" ::"l"(qrow + 32 * c));
+            }
 #pragma unroll 1
             for (int c = 0; c < kPHd / 32; ++c) {
                 float hi[32], lo[32];
@@ -165,26 +174,41 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_tc_pipe_kernel(const PAr
             float s[32];
             tc::ld32(tmem + lane_off + scol, s);
             tc::wait_ld();
-            float mt = m;
+            // Raw scores; masked keys become -inf.  Only the diagonal tiles
+            // (and a last tile past kv_end) mask anything, so a warp whose
+            // 32 rows all see the whole tile skips the test.  Max and sum run
+            // as four independent chains so the tile is latency-light.
+            float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+            if (__all_sync(0xffffffffu, k0 + kPKeys - 1 <= qp && k0 + kPKeys <= kv_end)) {
 #pragma unroll
-            for (int c = 0; c < 32; ++c) {
-                const int key = k0 + c;
-                s[c] = (key <= qp && key < kv_end) ? s[c] * a.scale_log2 : -INFINITY;
-                mt = fmaxf(mt, s[c]);
+                for (int c = 0; c < 32; ++c) mx[c & 3] = fmaxf(mx[c & 3], s[c]);
+            } else {
+#pragma unroll
+                for (int c = 0; c < 32; ++c) {
+                    const int key = k0 + c;
+                    if (!(key <= qp && key < kv_end)) s[c] = -INFINITY;
+                    mx[c & 3] = fmaxf(mx[c & 3], s[c]);
+                }
             }
+            // scale_log2 > 0, so the scaled max is the max of the scaled scores
+            const float mt =
+                fmaxf(m, fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * a.scale_log2);
             const bool move = (m == -INFINITY) || (mt > m + kPMaxLag);
             const float alpha = move ? ((m == -INFINITY) ? 0.f : fast_exp2(m - mt)) : 1.f;
             if (move) m = mt;
-            float rs = 0.f;
+            // Key 0 is in every row's first tile, so m is finite from here
+            // on and a masked score gives exp2(-inf) = +0.
+            const float neg_m = -m;
+            float rsp[4] = {0.f, 0.f, 0.f, 0.f};
             float phi[32], plo[32];
 #pragma unroll
             for (int c = 0; c < 32; ++c) {
-                const float p = (s[c] == -INFINITY) ? 0.f : fast_exp2(s[c] - m);
-                rs += p;
+                const float p = fast_exp2(fmaf(s[c], a.scale_log2, neg_m));
+                rsp[c & 3] += p;
                 phi[c] = tc::tf32_hi(p);
                 plo[c] = p - phi[c];
             }
-            l = l * alpha + rs;
+            l = l * alpha + ((rsp[0] + rsp[1]) + (rsp[2] + rsp[3]));
             tc::st32(tmem + lane_off + scol, phi);
             tc::st32(tmem + lane_off + scol + 32, plo);
             // O holds PV(0..j-1): rescale rows whose max moved, once PV(j-1)
@@ -349,13 +373,18 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_tc_pipe_kernel(const PAr
             }
             __syncwarp();
         };
-        auto issue_pv = [&](int j) {  // O += P(j) V(j)
+        // O += P(j) V(j): the two terms that read P hi (Phi Vhi, Phi Vlo)
+        // first, then Plo Vhi.  The commit between them frees the S columns
+        // (where P hi lives) for S(j+2), which then queues on the tensor core
+        // behind the P-lo products instead of waiting for the pipe to drain.
+        auto issue_pv = [&](int j) {
             const int b = j & 1;
             const uint32_t scol = kPColS + 64u * b;
             const uint64_t dv = b ? dvhi[1] : dvhi[0];
             if (leader) {
 #pragma unroll
                 for (int term = 0; term < 3; ++term) {
+                    if (term == 2) tc::commit(&bars.ph_free[b]);
 #pragma unroll
                     for (int kk = 0; kk < kPKeys / 8; ++kk) {
                         const uint64_t bdesc = dv + (term == 1 ? kLoStep : 0) + uint64_t(kk * 2);
@@ -368,7 +397,8 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_tc_pipe_kernel(const PAr
             __syncwarp();
         };
         // Issue whichever step is ready: S(j) once tile j's K operands are
-        // converted and PV(j-2) has released S/P buffer j%2; PV(j) once the
+        // converted and PV(j-2)'s P-hi terms have released buffer j%2's S
+        // columns; PV(j) once the
         // softmax has written P(j) and tile j's V operands are converted; the
         // copy of tile j+2 once the converters have taken tile j from staging.  Every test is of the next phase of
         // its barrier only (the one before it was observed), so parities
@@ -380,7 +410,7 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_tc_pipe_kernel(const PAr
             if (s_issued < n_kt && s_issued <= pv_issued + 1) {
                 const int j = s_issued, b = j & 1;
                 bool ready = mbar_test(&bars.k_full[b], par(j));
-                if (ready && j >= 2) ready = mbar_test(&bars.op_empty[b], par(j - 2));
+                if (ready && j >= 2) ready = mbar_test(&bars.ph_free[b], par(j - 2));
                 if (__all_sync(0xffffffffu, ready)) {
                     tc::fence_after_sync();
                     issue_s(j);
@@ -421,6 +451,7 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_tc_pipe_kernel(const PAr
             const int ls = s_issued - 1 - ((s_issued - 1 - b) & 1);      // last S into b
             if (ls >= 0) (void)mbar_wait(&bars.s_full[b], par(ls));
             const int lp = pv_issued - 1 - ((pv_issued - 1 - b) & 1);    // last PV on b
+            if (lp >= 0) (void)mbar_wait(&bars.ph_free[b], par(lp));
             if (lp >= 0) (void)mbar_wait(&bars.op_empty[b], par(lp));
             const int lt = staged - 1 - ((staged - 1 - b) & 1);          // last copy into b
             if (lt >= 0) (void)mbar_wait(&bars.st_full[b], par(lt));

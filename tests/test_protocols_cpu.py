@@ -10,8 +10,9 @@ written for that item and rewritten only after its readers are done.
 
   prefill_tc_pipe.cu  softmax warps / converter warps (K and V operands of a
                       tile in two steps) / one issuing lane; the issuer takes
-                      whichever of S(j), PV(j), copy(j) is ready; MMAs
-                      complete in issue order.
+                      whichever of S(j), PV(j), copy(j) is ready; PV(j) is
+                      its P-hi products then its P-lo products, with a commit
+                      between them; MMAs complete in issue order.
   engine_kernels.cu   gemv_q8_stream_kernel: dot warps / copy producer /
                       chain warp over (row block, chunk) items.
 """
@@ -40,16 +41,18 @@ def run_prefill(n_kt, seed, rescale_prob, n_conv=8):
     """prefill_tc_pipe_kernel.  Converter warps turn staged tile j into K and
     V operand tiles of buffer j%2 in two steps: K once S(j-2) has read K of
     that buffer (s_full), V once PV(j-2) has read V (op_empty); k_full and
-    v_full tell the issuer.  S(j) needs K(j) and the S/P TMEM buffer freed by
-    PV(j-2); PV(j) needs P(j) and V(j)."""
+    v_full tell the issuer.  S(j) needs K(j) and the S columns of its TMEM
+    buffer (where P(j-2) hi lives) freed by PV(j-2)'s P-hi products (ph_free);
+    PV(j) needs P(j) and V(j).  P(j) lo goes into columns PV(j-2)'s P-lo
+    products read, which in-order completion has finished before S(j)."""
     R = random.Random(seed)
     B = {}
     for b in (0, 1):
         for k, c in (("stf", 1), ("ste", n_conv), ("kf", n_conv), ("vf", n_conv), ("ope", 1),
-                     ("sf", 1), ("pf", 4)):
+                     ("sf", 1), ("pf", 4), ("phf", 1)):
             B[(k, b)] = Bar(c)
-    st = {"stage": {}, "opK": {}, "opV": {}, "S": {}, "P": {}, "O": 0, "sdone": set(),
-          "pvdone": set()}
+    st = {"stage": {}, "opK": {}, "opV": {}, "S": {}, "P": {}, "Plo": {}, "O": 0,
+          "sdone": set(), "phdone": set(), "pvdone": set()}
     mma, cps = [], []
     sm = [{"j": 0, "ph": 0} for _ in range(4)]
     cv = [{"j": 0, "ph": 0} for _ in range(n_conv)]
@@ -83,7 +86,7 @@ def run_prefill(n_kt, seed, rescale_prob, n_conv=8):
                 acts.append(("cvV", w))
         ns, np_, sg = iss["ns"], iss["np"], iss["staged"]
         if ns < n_kt and ns <= np_ + 1 and B[("kf", ns & 1)].ready(ns >> 1) and \
-                (ns < 2 or B[("ope", ns & 1)].ready((ns - 2) >> 1)):
+                (ns < 2 or B[("phf", ns & 1)].ready((ns - 2) >> 1)):
             acts.append(("S",))
         if np_ < ns and B[("pf", np_ & 1)].ready(np_ >> 1) and B[("vf", np_ & 1)].ready(np_ >> 1):
             acts.append(("PV",))
@@ -105,8 +108,10 @@ def run_prefill(n_kt, seed, rescale_prob, n_conv=8):
             w, j = a[1], sm[a[1]]["j"]
             if a[2]:
                 assert st["O"] == j  # O holds PV(0..j-1) when it is rescaled
+            assert j < 2 or (j - 2) in st["pvdone"]  # PV(j-2) has read P lo
             st["P"][(j & 1, w)] = j
             st["S"][(j & 1, w)] = ("P", j)
+            st["Plo"][(j & 1, w)] = j
             B[("pf", j & 1)].arrive()
             sm[w]["j"] += 1
             sm[w]["ph"] = 0
@@ -133,13 +138,17 @@ def run_prefill(n_kt, seed, rescale_prob, n_conv=8):
             j = iss["ns"]
             assert all(st["opK"].get((j & 1, w)) == j for w in range(n_conv))
             assert all(st["P"].get((j & 1, w)) in (None, j - 2) for w in range(4))
+            # S(j) writes the S columns: the products that read P(j-2) hi there
+            # must have completed, not merely be queued ahead of it
+            assert ("PVh", j - 2) not in mma
             mma.append(("S", j))
             iss["ns"] += 1
         elif a[0] == "PV":
             j = iss["np"]
             assert all(st["P"].get((j & 1, w)) == j for w in range(4))
             assert all(st["opV"].get((j & 1, w)) == j for w in range(n_conv))
-            mma.append(("PV", j))
+            mma.append(("PVh", j))
+            mma.append(("PVl", j))
             iss["np"] += 1
         elif a[0] == "stage":
             cps.append(iss["staged"])
@@ -149,12 +158,19 @@ def run_prefill(n_kt, seed, rescale_prob, n_conv=8):
             if kind == "S":
                 # its operands were not rewritten while it was in flight
                 assert all(st["opK"].get((j & 1, w)) == j for w in range(n_conv))
+                assert j < 2 or (j - 2) in st["phdone"]  # P(j-2) hi was read
                 for w in range(4):
                     st["S"][(j & 1, w)] = ("S", j)
                 st["sdone"].add(j)
                 B[("sf", j & 1)].arrive()
-            else:
+            elif kind == "PVh":  # Phi Vhi + Phi Vlo, then the ph_free commit
                 assert all(st["opV"].get((j & 1, w)) == j for w in range(n_conv))
+                assert all(st["S"].get((j & 1, w)) == ("P", j) for w in range(4))
+                st["phdone"].add(j)
+                B[("phf", j & 1)].arrive()
+            else:  # Plo Vhi, then the op_empty commit
+                assert all(st["opV"].get((j & 1, w)) == j for w in range(n_conv))
+                assert all(st["Plo"].get((j & 1, w)) == j for w in range(4))
                 assert st["O"] == j
                 st["O"] = j + 1
                 st["pvdone"].add(j)
