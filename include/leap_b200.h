@@ -408,6 +408,13 @@ LEAP_API int leap_op_qmatmul_fused(void *stream, float *y, const float *x,
  *     pipeline, warp-specialised (dot warps, a copy producer, a chain warp;
  *     the default).  All compute the same bits. */
 LEAP_API int leap_op_set_q8_gemv(int impl);
+/* W8A8 GEMM kernel selection for T > 1, the prompt chunks of
+ * leap_engine_prefill / leap_op_qmatmul (process-wide; tests/benchmarks):
+ * 0 = CUDA-core dp4a tiles, 1 = tcgen05 kind::i8 tensor-core tiles whose
+ * int32 group dots feed the same ordered FP32 chain (the default; used where
+ * n % 256 == 0 and the operands are 16-byte aligned).  Both compute the bits
+ * of QuantizedTransformer.cpp:359-652. */
+LEAP_API int leap_op_set_q8_gemm(int impl);
 /* Greedy sampling (Sampler.cpp:20-120 at temperature 0): index of the
  * first maximum in the reference's scan order. */
 LEAP_API int leap_op_argmax(void *stream, int *token, const float *v, int n);

@@ -126,6 +126,7 @@ SIGNATURES: dict[str, tuple] = {
     "leap_pp_abort": (c_int, [c_void_p]),
     "leap_pp_destroy": (c_int, [c_void_p]),
     "leap_op_set_q8_gemv": (c_int, [c_int]),
+    "leap_op_set_q8_gemm": (c_int, [c_int]),
 }
 
 _lock = threading.Lock()

@@ -455,7 +455,7 @@ int linear_mat(leap_engine *e, float *y, const float *x, const Mat &w, int row0,
     const int n = w.cols;
     if (w.f) return gemm_f32(e->stream, y, x, w.f + size_t(row0) * n, n, rows, T, res);
     return gemm_q8(e->stream, y, e->baq, e->bas, w.q + size_t(row0) * n,
-                   w.s + size_t(row0) * n / e->cfg.group_size, n, rows, T, res);
+                   w.s + size_t(row0) * n / e->cfg.group_size, n, rows, T, res, e->attn->d_err);
 }
 
 // One token through the local layers (run_layer, FloatTransformer.cpp:384-749;
@@ -908,6 +908,16 @@ int leap_op_set_q8_gemv(int impl) {
     }
     leap::eng::g_q8_slice = impl == 0;
     leap::eng::g_q8_tma = impl == 2;
+    return LEAP_OK;
+}
+
+int leap_op_set_q8_gemm(int impl) {
+    leap::clear_error();
+    if (impl < 0 || impl > 1) {
+        leap::set_error("q8 gemm impl %d (0 CUDA-core dp4a, 1 tcgen05 kind::i8)", impl);
+        return LEAP_ERR_INVALID;
+    }
+    leap::eng::g_q8_gemm_tc = impl == 1;
     return LEAP_OK;
 }
 

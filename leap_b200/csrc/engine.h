@@ -28,8 +28,16 @@ int gemv_q8_fused(cudaStream_t st, float *y, const float *x, const float *nw, in
                   int *err = nullptr);
 extern bool g_q8_slice;  // int8 GEMV: sliced one-row-per-lane kernel (else register-staged)
 extern bool g_q8_tma;    // int8 GEMV: persistent bulk-copy kernel (default; takes precedence)
+// int8 GEMM (prompt chunks, T tokens): the tcgen05 kind::i8 kernel
+// (gemm_q8_tc.cu) where gemm_q8_tc_supported() holds and g_q8_gemm_tc is
+// set (the default), else the CUDA-core dp4a kernel; both give the same bits.
+extern bool g_q8_gemm_tc;
+bool gemm_q8_tc_supported(const int8_t *xq, const float *xs, const int8_t *wq, const float *ws,
+                          int n, int T);
+int gemm_q8_tc(cudaStream_t st, float *y, const int8_t *xq, const float *xs, const int8_t *wq,
+               const float *ws, int n, int d, int T, const float *res, int *err);
 int gemm_q8(cudaStream_t st, float *y, const int8_t *xq, const float *xs, const int8_t *wq,
-            const float *ws, int n, int d, int T, const float *res);
+            const float *ws, int n, int d, int T, const float *res, int *err = nullptr);
 // y = W . a (+ res); a = x, or rmsnorm(x, nw) formed in the GEMV's prologue
 // (same bits as rmsnorm followed by the GEMV; xb: a scratch row for the
 // unfused route, used when x is misaligned or too long for shared memory).

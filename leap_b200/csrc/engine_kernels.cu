@@ -1182,8 +1182,12 @@ int gemv_q8(cudaStream_t st, float *y, const int8_t *xq, const float *xs, const 
                       dim3(kGemvWarps * 32), smem, st, y, xq, xs, wq, ws, n, d, res);
 }
 
+bool g_q8_gemm_tc = true;
+
 int gemm_q8(cudaStream_t st, float *y, const int8_t *xq, const float *xs, const int8_t *wq,
-            const float *ws, int n, int d, int T, const float *res) {
+            const float *ws, int n, int d, int T, const float *res, int *err) {
+    if (g_q8_gemm_tc && gemm_q8_tc_supported(xq, xs, wq, ws, n, T))
+        return gemm_q8_tc(st, y, xq, xs, wq, ws, n, d, T, res, err);
     dim3 grid((d + kGR - 1) / kGR, (T + kGT - 1) / kGT);
     gemm_q8_kernel<<<grid, kGThreads, 0, st>>>(y, xq, xs, wq, ws, n, d, T, res);
     return cuda_status(cudaGetLastError(), "gemm_q8");

@@ -15,6 +15,8 @@ written for that item and rewritten only after its readers are done.
                       between them; MMAs complete in issue order.
   engine_kernels.cu   gemv_q8_stream_kernel: dot warps / copy producer /
                       chain warp over (row block, chunk) items.
+  gemm_q8_tc.cu       gemm_q8_tc_kernel: TMA producer (two groups per stage) /
+                      MMA issuer (one TMEM buffer per group) / epilogue warps.
 """
 import random
 
@@ -229,6 +231,94 @@ def run_gemv(items, seed, n_stages=3, n_dot=8):
             stage[it % n_stages] = it
             full[it % n_stages].arrive()
     return "livelock"
+
+
+def run_gemm_tc(ng, seed, n_stages=4, n_buf=4, n_epi=8):
+    """gemm_q8_tc_kernel.  The producer loads K slice c (groups 2c, 2c+1)
+    into stage c % S once the MMAs of slice c - S have completed (empty);
+    the issuer, for group g, waits for its slice (full, at even g) and for
+    the epilogue to have read buffer g % NB's previous group (dempty), then
+    issues two products into that buffer and commits dfull, and commits
+    empty after a slice's last group; the epilogue warps read each group's
+    buffer in order and release it."""
+    R = random.Random(seed)
+    nch = (ng + 1) // 2
+    B = {}
+    for s_ in range(n_stages):
+        B[("full", s_)] = Bar(1)
+        B[("empty", s_)] = Bar(1)
+    for b in range(n_buf):
+        B[("dfull", b)] = Bar(1)
+        B[("dempty", b)] = Bar(n_epi)
+    stage, tmem = {}, {}
+    mma, cps = [], []
+    prod = {"c": 0}
+    iss = {"g": 0}
+    epi = [0] * n_epi
+    for _ in range(200000):
+        acts = []
+        c = prod["c"]
+        if c < nch and (c < n_stages or B[("empty", c % n_stages)].ready(c // n_stages - 1)):
+            acts.append(("copy",))
+        g = iss["g"]
+        if g < ng:
+            cc, b = g >> 1, g % n_buf
+            ok = (g & 1) or B[("full", cc % n_stages)].ready(cc // n_stages)
+            if ok and (g < n_buf or B[("dempty", b)].ready(g // n_buf - 1)):
+                acts.append(("mma",))
+        for w in range(n_epi):
+            ge = epi[w]
+            if ge < ng and B[("dfull", ge % n_buf)].ready(ge // n_buf):
+                acts.append(("epi", w))
+        if mma:
+            acts.append(("done",))
+        acts += [("land",)] * len(cps)
+        if not acts:
+            ok = iss["g"] >= ng and all(e >= ng for e in epi) and not mma and not cps
+            return "ok" if ok else "deadlock"
+        a = R.choice(acts)
+        if a[0] == "copy":
+            c = prod["c"]
+            # the slice this copy overwrites has no product in flight
+            assert all(k != ("slice", c - n_stages) for k in mma)
+            cps.append(c)
+            prod["c"] += 1
+        elif a[0] == "land":
+            c = cps.pop(R.randrange(len(cps)))
+            stage[c % n_stages] = c
+            B[("full", c % n_stages)].arrive()
+        elif a[0] == "mma":
+            g = iss["g"]
+            cc, b = g >> 1, g % n_buf
+            assert stage.get(cc % n_stages) == cc  # its slice has landed
+            mma.append(("group", g))
+            if (g & 1) or g == ng - 1:
+                mma.append(("slice", cc))
+            iss["g"] += 1
+        elif a[0] == "done":  # products complete in issue order
+            kind, v = mma.pop(0)
+            if kind == "group":
+                b = v % n_buf
+                # the buffer's previous group was read by every epilogue warp
+                assert all(e >= v - n_buf + 1 for e in epi)
+                assert stage.get((v >> 1) % n_stages) == v >> 1
+                tmem[b] = v
+                B[("dfull", b)].arrive()
+            else:
+                B[("empty", v % n_stages)].arrive()
+        else:
+            w = a[1]
+            ge = epi[w]
+            assert tmem.get(ge % n_buf) == ge
+            epi[w] += 1
+            B[("dempty", ge % n_buf)].arrive()
+    return "livelock"
+
+
+@pytest.mark.parametrize("ng", [1, 2, 3, 4, 5, 8, 9, 17])
+def test_gemm_tc_protocol(ng):
+    for seed in range(200):
+        assert run_gemm_tc(ng, seed) == "ok", (ng, seed)
 
 
 @pytest.mark.parametrize("n_kt", [1, 2, 3, 4, 7, 10])

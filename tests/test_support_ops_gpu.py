@@ -181,6 +181,43 @@ def test_qmatmul_gemm_equals_gemv_rows(cuda, T):
     assert np.array_equal(y[-1], (res[-1] + ref).astype(np.float32))
 
 
+@pytest.mark.parametrize("n,d,T", [(4096, 6144, 64), (14336, 4096, 100), (4096, 200, 130),
+                                   (256, 128, 2), (8192, 1024, 512)])
+def test_qmatmul_gemm_tensor_core_equals_dp4a(cuda, n, d, T):
+    """The tcgen05 kind::i8 GEMM (impl 1, the default) and the CUDA-core
+    dp4a GEMM (impl 0) give the same bits, with and without a residual, on
+    ragged row and token tiles; sampled outputs equal the port's chain."""
+    r = np.random.default_rng(n + d + T)
+    x = r.standard_normal((T, n)).astype(np.float32)
+    w = (r.standard_normal((d, n)) * 0.02).astype(np.float32)
+    res = r.standard_normal((T, d)).astype(np.float32)
+    wq, ws = oracle.quantize(w.reshape(-1))
+    wq_d, ws_d = _dev(wq), _dev(ws)
+    xq_d, xs_d = _quantize_dev(_dev(x))
+    res_d = _dev(res)
+    out = {}
+    try:
+        for impl in (0, 1):
+            check(lib().leap_op_set_q8_gemm(impl))
+            out[impl] = (_qmm(xq_d, xs_d, wq_d, ws_d, n, d, T).cpu().numpy(),
+                         _qmm(xq_d, xs_d, wq_d, ws_d, n, d, T, res_d).cpu().numpy())
+    finally:
+        check(lib().leap_op_set_q8_gemm(1))  # the library default
+    assert np.array_equal(out[1][0], out[0][0])
+    assert np.array_equal(out[1][1], out[0][1])
+    for t in sorted({0, T // 2, T - 1}):
+        xq, xs = oracle.quantize(x[t])
+        ref = oracle.qmatmul(xq, xs, wq.reshape(d, n), ws.reshape(d, n // 64), threads=8)
+        assert np.array_equal(out[1][0][t], ref)
+        assert np.array_equal(out[1][1][t], (res[t] + ref).astype(np.float32))
+
+
+def test_qmatmul_gemm_impl_selection(cuda):
+    with pytest.raises(LeapError):
+        check(lib().leap_op_set_q8_gemm(2))
+    check(lib().leap_op_set_q8_gemm(1))
+
+
 def _mm(x_d, w_d, n, d, T, res=None):
     y = torch.empty((T, d), dtype=torch.float32, device="cuda")
     check(lib().leap_op_matmul(_s(), y.data_ptr(), x_d.data_ptr(), w_d.data_ptr(), n, d, T,
