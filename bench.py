@@ -913,6 +913,83 @@ def run_batched(args):
     emit(line)
 
 
+def run_qgemm(args):
+    """The W8A8 prompt-chunk GEMMs of one Llama-3-8B-shape layer (wq;wk;wv,
+    wo, w1;w3, w2) over T tokens through leap_op_qmatmul, the product the
+    engine's prefill runs per 512-token chunk (QuantizedTransformer.cpp:
+    359-652 per token).  One step = the four GEMMs; the weights are random
+    int8 with random group scales.  Metric: int8 TOP/s (2·n·d·T per GEMM).
+    The CUDA-core dp4a kernel is timed beside the tcgen05 one."""
+    import ctypes
+    import torch
+    from leap_b200._native import check, lib
+    dev = torch.device("cuda", 0)
+    T = args.qgemm
+    shapes = [("wqkv", 4096, 6144), ("wo", 4096, 4096), ("w13", 4096, 28672),
+              ("w2", 14336, 4096)]
+    g = torch.Generator(device=dev)
+    g.manual_seed(SEED)
+    mats = []
+    for _, n, d in shapes:
+        wq = torch.randint(-127, 128, (d, n), dtype=torch.int8, device=dev, generator=g)
+        ws = torch.rand(d, n // 64, device=dev, generator=g) * 1e-3
+        xq = torch.randint(-127, 128, (T, n), dtype=torch.int8, device=dev, generator=g)
+        xs = torch.rand(T, n // 64, device=dev, generator=g) * 1e-2
+        mats.append((n, d, wq, ws, xq, xs, torch.empty(T, d, device=dev)))
+    stream = torch.cuda.current_stream(dev)
+    s = ctypes.c_void_p(stream.cuda_stream)
+
+    def step():
+        for n, d, wq, ws, xq, xs, y in mats:
+            check(lib().leap_op_qmatmul(s, y.data_ptr(), xq.data_ptr(), xs.data_ptr(),
+                                        wq.data_ptr(), ws.data_ptr(), n, d, T, 64, None))
+
+    ops = sum(2.0 * n * d * T for _, n, d in shapes)
+    per = {}
+    clocks = None
+    try:
+        for impl, steps in ((0, max(2, args.steps // 10)), (1, args.steps)):
+            check(lib().leap_op_set_q8_gemm(impl))
+            for _ in range(max(args.warmup, 3)):
+                step()
+            torch.cuda.synchronize(dev)
+            sampler = ClockSampler(0)
+            if impl == 1:
+                sampler.start()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(steps):
+                step()
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+            if impl == 1:
+                clocks = sampler.stop()
+            per[impl] = e0.elapsed_time(e1) / steps
+    finally:
+        check(lib().leap_op_set_q8_gemm(1))
+    ms = per[1]
+    tops = ops / (ms / 1e3) / 1e12
+    peak = 2 * 1622.9
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            peak = 2 * float(json.load(f)["bf16_tflops"])
+    emit({"metric": "W8A8 prompt GEMM TOP/s (int8)", "value": round(tops, 1), "unit": "TOP/s",
+          "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+          "higher_is_better": True, "dtype": "int8 x int8 -> s32, f32 chain",
+          "data": "synthetic (random int8 weights and activations, random scales)",
+          "config": {"workload": f"the 4 W8A8 GEMMs of one Llama-3-8B-shape layer over {T} "
+                                 "prompt tokens (wqkv, wo, w13, w2)", "tokens": T,
+                     "l2": "inputs > L2: 219 MB of int8 weights per step"},
+          "cuda_core_dp4a": {"value": round(ops / (per[0] / 1e3) / 1e12, 1), "unit": "TOP/s",
+                             "ms_per_step": round(per[0], 4)},
+          "roofline": {"bound": "tensor", "achieved": round(tops, 1), "peak": peak,
+                       "peak_kind": "2 x measured bf16 dense (int8 rate)", "unit": "TOP/s",
+                       "frac": round(tops / peak, 4)},
+          "gpu_launches": 4 * args.steps, "clocks": clocks})
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -946,6 +1023,8 @@ def main():
                     help="stage transport for --model on N > 1 ranks")
     ap.add_argument("--no-pipeline", action="store_true",
                     help="skip the 8B W8A8 layer-range pipeline of the default line")
+    ap.add_argument("--qgemm", type=int, default=0,
+                    help="benchmark the W8A8 prompt GEMMs of one 8B layer over this many tokens")
     args = ap.parse_args()
     _keep_stdout_for_result()
     args.steps_given = args.steps is not None
@@ -964,6 +1043,8 @@ def main():
         run_batched(args)
     elif args.prefill:
         run_prefill(args)
+    elif args.qgemm:
+        run_qgemm(args)
     else:
         run_gpu_arm(args)
 

@@ -84,12 +84,13 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, i
         : "memory");
 }
 
-// float(i) for |i| < 2^22, exactly: i added to the integer image of 1.5 * 2^23
-// lands on the float 1.5 * 2^23 + i (unit spacing there), then 1.5 * 2^23 is
-// subtracted.  Two full-rate instructions instead of a conversion.
-__device__ __forceinline__ float small_int_to_float(int i) {
-    return __int_as_float(i + 0x4B400000) - 12582912.0f;
-}
+// float(i) for |i| < 2^22, exactly: i added to the integer image of
+// kMagic = 1.5 * 2^23 lands on the float kMagic + i (unit spacing there), and
+// subtracting kMagic leaves i.  A group dot is at most 64 * 128 * 128 = 2^20
+// in magnitude.  An integer add and a (packed) float add instead of a
+// conversion instruction.
+constexpr float kMagic = 12582912.0f;
+__device__ __forceinline__ float magic_image(int i) { return __int_as_float(i + 0x4B400000); }
 
 __global__ void __launch_bounds__(kQThreads, 2)
 gemm_q8_tc_kernel(const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tmx,
@@ -213,9 +214,9 @@ gemm_q8_tc_kernel(const __grid_constant__ CUtensorMap tmw, const __grid_constant
                 x[4 * i + 3] = xv.w;
             }
         };
-        float val[32];
+        float2 val[16];  // tokens (2i, 2i + 1)
 #pragma unroll
-        for (int i = 0; i < 32; ++i) val[i] = 0.f;
+        for (int i = 0; i < 16; ++i) val[i] = make_float2(0.f, 0.f);
         float wcur[kQGB], wnxt[kQGB], xnxt[kQGB];
         load_scales(0, wcur, xnxt);
 #pragma unroll
@@ -238,17 +239,23 @@ gemm_q8_tc_kernel(const __grid_constant__ CUtensorMap tmw, const __grid_constant
                         tc::fence_before_sync();
                         __syncwarp();
                         if (lane == 0) mbar_arrive(&dempty[b]);
-                        const float wsg = wcur[gg];
+                        // token pairs in packed FP32x2 instructions, each
+                        // half rounded exactly as the scalar fma / mul
+                        const float2 wsg = make_float2(wcur[gg], wcur[gg]);
+                        const float2 neg_c = make_float2(-kMagic, -kMagic);
                         const float4 *xr = reinterpret_cast<const float4 *>(sxw + gg * 32);
 #pragma unroll
                         for (int i4 = 0; i4 < 8; ++i4) {
                             const float4 x4 = xr[i4];
-                            const float xv[4] = {x4.x, x4.y, x4.z, x4.w};
+                            const float2 xp[2] = {make_float2(x4.x, x4.y), make_float2(x4.z, x4.w)};
 #pragma unroll
-                            for (int e = 0; e < 4; ++e) {
-                                const int t = 4 * i4 + e;
-                                const float dot = small_int_to_float(__float_as_int(dv[t]));
-                                val[t] = fmaf(dot, __fmul_rn(wsg, xv[e]), val[t]);
+                            for (int e = 0; e < 2; ++e) {
+                                const int t = 4 * i4 + 2 * e;
+                                const float2 dot = __fadd2_rn(
+                                    make_float2(magic_image(__float_as_int(dv[t])),
+                                                magic_image(__float_as_int(dv[t + 1]))),
+                                    neg_c);
+                                val[t / 2] = __ffma2_rn(dot, __fmul2_rn(wsg, xp[e]), val[t / 2]);
                             }
                         }
                     }
@@ -271,7 +278,8 @@ gemm_q8_tc_kernel(const __grid_constant__ CUtensorMap tmw, const __grid_constant
                     const int tt = t0 + 32 * h + t;
                     if (tt < T) {
                         const size_t o = size_t(tt) * d + row;
-                        y[o] = res ? __fadd_rn(res[o], val[t]) : val[t];
+                        const float v = (t & 1) ? val[t / 2].y : val[t / 2].x;
+                        y[o] = res ? __fadd_rn(res[o], v) : v;
                     }
                 }
             }
