@@ -490,14 +490,16 @@ def run_prefill(args):
             peak = float(json.load(f)["bf16_tflops"])
     line = {"metric": "causal prefill TFLOP/s (logical FP32)", "value": round(tflops, 2),
             "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(ms, 4), "higher_is_better": True, "dtype": "f32 (3xTF32)"
-            if args.prefill_impl != 1 else "f32",
+            "ms_per_step": round(ms, 4), "higher_is_better": True,
+            "dtype": {1: "f32", 3: "f32 (TF32 + BF16 corrections)"}.get(args.prefill_impl,
+                                                                        "f32 (3xTF32)"),
             "config": {"workload": f"config4: causal prefill L={L}, Llama-3-8B heads, batch 1",
                        "seq_len": L, "impl": {0: "tcgen05 3xTF32 pipelined", 1: "CUDA-core FP32",
-                                2: "tcgen05 3xTF32 serial"}[args.prefill_impl]},
+                                2: "tcgen05 3xTF32 serial",
+                                3: "tcgen05 TF32 + BF16 corrections pipelined"}[args.prefill_impl]},
             "roofline": {"bound": "tensor", "achieved": round(tflops, 2),
                          "tensor_tflops_issued": round(3 * tflops, 2)
-                         if args.prefill_impl != 1 else None,
+                         if args.prefill_impl in (0, 2) else None,
                          "peak": peak, "peak_kind": "measured bf16 dense (TF32 is half)",
                          "unit": "TFLOP/s", "frac": round(tflops / peak, 4)}}
     ctx.close()
@@ -1007,8 +1009,9 @@ def main():
                     help="no programmatic dependent launch between layers")
     ap.add_argument("--prefill", type=int, default=0,
                     help="benchmark config 4 (causal prefill of this many tokens) instead")
-    ap.add_argument("--prefill-impl", type=int, default=0,
-                    help="0 tcgen05 3xTF32 pipelined, 1 CUDA-core FP32, 2 tcgen05 3xTF32 serial")
+    ap.add_argument("--prefill-impl", type=int, default=3,
+                    help="0 tcgen05 3xTF32 pipelined, 1 CUDA-core FP32, 2 tcgen05 3xTF32 serial, "
+                         "3 tcgen05 TF32 + BF16 corrections pipelined")
     ap.add_argument("--layers", type=int, default=N_LAYERS)
     ap.add_argument("--ctx", type=int, default=CTX)
     ap.add_argument("--batched", action="store_true",

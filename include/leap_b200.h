@@ -340,10 +340,13 @@ LEAP_API int leap_engine_prefill(leap_engine *e, const int *tokens, int n,
                                  int pos0, int *next_token);
 
 /* Prefill kernel selection (for tests and benchmarks):
- *   0 = default: tensor-core 3xTF32, software-pipelined across warp roles
+ *   0 = tensor-core 3xTF32, software-pipelined across warp roles
  *       (softmax, operand conversion and MMA issue overlap),
  *   1 = CUDA-core FP32 path,
- *   2 = tensor-core 3xTF32, one tile at a time (no overlap). */
+ *   2 = tensor-core 3xTF32, one tile at a time (no overlap),
+ *   3 = default: as 0 with the two correction products (hi*lo, lo*hi) in
+ *       BF16 (kind::f16, K = 16): 40 instead of 60 tensor-core instructions
+ *       per 32-key tile, about 2^-19 relative per product. */
 LEAP_API int leap_set_prefill_impl(leap_ctx *ctx, int impl);
 
 /* ---- support ops of the layer, one kernel each --------------------------

@@ -213,7 +213,8 @@ class AttentionContext:
         check(lib().leap_set_overlap(self.handle, int(bool(enable))))
 
     def set_prefill_impl(self, impl: int) -> None:
-        """0 = tensor-core 3xTF32 kernel pipelined across warp roles (default),
+        """0 = tensor-core 3xTF32 kernel pipelined across warp roles,
         1 = CUDA-core FP32 kernel, 2 = tensor-core 3xTF32 kernel, one tile at
-        a time."""
+        a time, 3 = the pipelined kernel with its two correction products in
+        BF16 (the default)."""
         check(lib().leap_set_prefill_impl(self.handle, impl))

@@ -563,7 +563,7 @@ int leap_attn_prefill(leap_ctx *c, int slot, int layer, int pos0, int n_tok, con
 int leap_set_prefill_impl(leap_ctx *c, int impl) {
     leap::clear_error();
     LEAP_CHECK_CTX(c);
-    if (impl < 0 || impl > 2) {
+    if (impl < 0 || impl > 3) {
         leap::set_error("prefill impl %d unknown", impl);
         return LEAP_ERR_INVALID;
     }

@@ -63,7 +63,7 @@ struct leap_ctx {
     // prefill scratch (rotated q), grown on demand
     float *d_qrot = nullptr;
     size_t qrot_cap = 0;  // floats
-    int prefill_impl = 0;
+    int prefill_impl = 3;  // see leap_set_prefill_impl
 
     size_t device_bytes = 0;
 };

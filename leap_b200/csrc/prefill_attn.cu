@@ -245,7 +245,7 @@ int launch_prefill_tc(leap_ctx *c, const float *qrot, const float *kc, const flo
 // the same product, software-pipelined across warp roles (prefill_tc_pipe.cu):
 // the default
 int launch_prefill_tc_pipe(leap_ctx *c, const float *qrot, const float *kc, const float *vc,
-                           float *out, int pos0, int n_tok);
+                           float *out, int pos0, int n_tok, bool bf16_corrections);
 
 int launch_prefill(leap_ctx *c, int slot, int layer, int pos0, int n_tok, const float *q,
                    const float *k, const float *v, float *out) {
@@ -272,10 +272,11 @@ int launch_prefill(leap_ctx *c, int slot, int layer, int pos0, int n_tok, const 
             c->n_heads, c->n_kv);
     if (int st = cuda_status(cudaGetLastError(), "prefill_rope_append launch")) return st;
 
-    if (c->prefill_impl == 0 || c->prefill_impl == 2) {
-        const int st = c->prefill_impl == 0
-                           ? launch_prefill_tc_pipe(c, c->d_qrot, kc, vc, out, pos0, n_tok)
-                           : launch_prefill_tc(c, c->d_qrot, kc, vc, out, pos0, n_tok);
+    if (c->prefill_impl != 1) {
+        const int st = c->prefill_impl == 2
+                           ? launch_prefill_tc(c, c->d_qrot, kc, vc, out, pos0, n_tok)
+                           : launch_prefill_tc_pipe(c, c->d_qrot, kc, vc, out, pos0, n_tok,
+                                                    c->prefill_impl == 3);
         if (st != LEAP_ERR_INVALID) return st;
         clear_error();  // shape not covered by the tensor-core kernel
     }

@@ -22,8 +22,18 @@
 //                       S/P hi buffer b at 384+64b, P lo at 384+64b+32;
 //   shared memory: per buffer b, K hi/lo [32][128] and V^T hi/lo [128][32]
 //                  (4 x 16 KB) and FP32 staging K, V [32][128] (2 x 16 KB).
-// Products are hi*hi + hi*lo + lo*hi (3xTF32, ~2^-21 relative).  The running
-// max moves only when a row's max grows by more than 2^8 (see prefill_tc.cu).
+// Products are hi*hi + hi*lo + lo*hi (3xTF32, ~2^-21 relative).  With BFC the
+// two correction products (hi*lo, lo*hi) run as BF16 kind::f16 products of
+// K = 16 instead (the hi and lo parts rounded to BF16, ~2^-19 relative per
+// product, FP32's exponent range): 40 instead of 60 tensor-core instructions
+// per 32-key tile, in the same TMEM columns and shared-memory tiles:
+//   TMEM: Q hi (TF32) [0,128), Q hi (BF16 pairs) [128,192), Q lo (BF16 pairs)
+//         [192,256); P hi (TF32) over S, P hi | P lo (BF16 pairs) at +32 / +48;
+//   K operands: hi (TF32, 16 KB), hi (BF16, 8 KB), lo (BF16, 8 KB);
+//   V^T operands: hi (TF32, 16 KB), hi | lo (BF16) in the two halves of each
+//         128-byte row (16 KB).
+// The running max moves only when a row's max grows by more than 2^8 (see
+// prefill_tc.cu).
 // All hand-offs are mbarriers; every wait is bounded and a timeout sets the
 // error word after draining what is in flight.
 #include "common.cuh"
@@ -78,7 +88,7 @@ struct PBars {
 
 __device__ __forceinline__ uint32_t par(int j) { return uint32_t(j >> 1) & 1u; }
 
-template <int G>
+template <int G, bool BFC>
 __global__ void __launch_bounds__(kPThreads, 1) prefill_tc_pipe_kernel(const PArgs a) {
     constexpr int BT = kPRows / G;  // tokens per CTA
     extern __shared__ unsigned char smem_raw[];
@@ -155,7 +165,18 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_tc_pipe_kernel(const PAr
                     }
                 }
                 tc::st32(tmem + lane_off + kPColQhi + 32 * c, hi);
-                tc::st32(tmem + lane_off + kPColQlo + 32 * c, lo);
+                if (BFC) {
+                    uint32_t h16[16], l16[16];
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        h16[i] = tc::pack_bf16x2(hi[2 * i], hi[2 * i + 1]);
+                        l16[i] = tc::pack_bf16x2(lo[2 * i], lo[2 * i + 1]);
+                    }
+                    tc::st16u(tmem + lane_off + kPColQlo + 16 * c, h16);
+                    tc::st16u(tmem + lane_off + kPColQlo + 64 + 16 * c, l16);
+                } else {
+                    tc::st32(tmem + lane_off + kPColQlo + 32 * c, lo);
+                }
             }
             tc::wait_st();
             tc::fence_before_sync();
@@ -210,7 +231,17 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_tc_pipe_kernel(const PAr
             }
             l = l * alpha + ((rsp[0] + rsp[1]) + (rsp[2] + rsp[3]));
             tc::st32(tmem + lane_off + scol, phi);
-            tc::st32(tmem + lane_off + scol + 32, plo);
+            if (BFC) {
+                float p16[32];  // BF16 pairs: P hi in cells 0-15, P lo in 16-31
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    p16[i] = __uint_as_float(tc::pack_bf16x2(phi[2 * i], phi[2 * i + 1]));
+                    p16[16 + i] = __uint_as_float(tc::pack_bf16x2(plo[2 * i], plo[2 * i + 1]));
+                }
+                tc::st32(tmem + lane_off + scol + 32, p16);
+            } else {
+                tc::st32(tmem + lane_off + scol + 32, plo);
+            }
             // O holds PV(0..j-1): rescale rows whose max moved, once PV(j-1)
             // has landed (PV(j) is issued only after this warp's arrival below)
             if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
@@ -285,7 +316,15 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_tc_pipe_kernel(const PAr
                 h.w = tc::tf32_hi(v.w); w.w = v.w - h.w;
                 const uint32_t off = tc::sw128_offset(n, d, kPKeys);
                 *reinterpret_cast<float4 *>(base + kPOffKhi(b) + off) = h;
-                *reinterpret_cast<float4 *>(base + kPOffKlo(b) + off) = w;
+                if (BFC) {
+                    const uint32_t o16 = tc::sw128_offset_b16(n, d, kPKeys);
+                    *reinterpret_cast<uint2 *>(base + kPOffKlo(b) + o16) =
+                        make_uint2(tc::pack_bf16x2(h.x, h.y), tc::pack_bf16x2(h.z, h.w));
+                    *reinterpret_cast<uint2 *>(base + kPOffKlo(b) + kPOpBytes / 2 + o16) =
+                        make_uint2(tc::pack_bf16x2(w.x, w.y), tc::pack_bf16x2(w.z, w.w));
+                } else {
+                    *reinterpret_cast<float4 *>(base + kPOffKlo(b) + off) = w;
+                }
             }
             fence_proxy_async_smem();  // K operand writes -> visible to the tensor core
             __syncwarp();
@@ -313,7 +352,17 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_tc_pipe_kernel(const PAr
                     h.w = tc::tf32_hi(x[3]); w.w = x[3] - h.w;
                     const uint32_t off = tc::sw128_offset(d, 4 * jg, kPHd);
                     *reinterpret_cast<float4 *>(base + kPOffVThi(b) + off) = h;
-                    *reinterpret_cast<float4 *>(base + kPOffVTlo(b) + off) = w;
+                    if (BFC) {
+                        // keys 0-31 of row d: hi in bytes 0-63, lo in 64-127
+                        *reinterpret_cast<uint2 *>(base + kPOffVTlo(b) +
+                                                   tc::sw128_offset_b16(d, 4 * jg, kPHd)) =
+                            make_uint2(tc::pack_bf16x2(h.x, h.y), tc::pack_bf16x2(h.z, h.w));
+                        *reinterpret_cast<uint2 *>(base + kPOffVTlo(b) +
+                                                   tc::sw128_offset_b16(d, kPKeys + 4 * jg, kPHd)) =
+                            make_uint2(tc::pack_bf16x2(w.x, w.y), tc::pack_bf16x2(w.z, w.w));
+                    } else {
+                        *reinterpret_cast<float4 *>(base + kPOffVTlo(b) + off) = w;
+                    }
                 }
             }
             fence_proxy_async_smem();  // V operand writes -> visible to the tensor core
@@ -346,6 +395,8 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_tc_pipe_kernel(const PAr
         };
         const uint32_t idesc_s = tc::idesc_tf32(kPRows, kPKeys);
         const uint32_t idesc_o = tc::idesc_tf32(kPRows, kPHd);
+        const uint32_t idesc_s16 = tc::idesc_bf16(kPRows, kPKeys);
+        const uint32_t idesc_o16 = tc::idesc_bf16(kPRows, kPHd);
         const uint64_t dkhi[2] = {tc::sw128_kmajor_desc(sbase + kPOffKhi(0)),
                                   tc::sw128_kmajor_desc(sbase + kPOffKhi(1))};
         const uint64_t dvhi[2] = {tc::sw128_kmajor_desc(sbase + kPOffVThi(0)),
@@ -359,14 +410,34 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_tc_pipe_kernel(const PAr
             const uint32_t scol = kPColS + 64u * b;
             const uint64_t dk = b ? dkhi[1] : dkhi[0];
             if (leader) {
+                if (BFC) {
 #pragma unroll
-                for (int term = 0; term < 3; ++term) {
+                    for (int kk = 0; kk < kPHd / 8; ++kk)  // Qhi Khi, TF32, K = 8
+                        tc::mma_tf32_ts(tmem + scol, tmem + kPColQhi + 8 * kk,
+                                        dk + uint64_t(((kk >> 2) * (kPKeys * 128) + (kk & 3) * 32) >> 4),
+                                        idesc_s, kk > 0 ? 1u : 0u);
+                    // BF16 K tiles follow the TF32 hi tile: hi at +16 KB, lo at +24 KB
 #pragma unroll
-                    for (int kk = 0; kk < kPHd / 8; ++kk) {
-                        const uint64_t bdesc = dk + (term == 1 ? kLoStep : 0) +
-                                               uint64_t(((kk >> 2) * (kPKeys * 128) + (kk & 3) * 32) >> 4);
-                        tc::mma_tf32_ts(tmem + scol, tmem + (term == 2 ? kPColQlo : kPColQhi) + 8 * kk,
-                                        bdesc, idesc_s, (term > 0 || kk > 0) ? 1u : 0u);
+                    for (int term = 1; term < 3; ++term) {
+#pragma unroll
+                        for (int kk = 0; kk < kPHd / 16; ++kk) {  // K = 16 per product
+                            const uint64_t bdesc = dk + kLoStep + (term == 1 ? kLoStep / 2 : 0) +
+                                uint64_t(((kk >> 2) * (kPKeys * 128) + (kk & 3) * 32) >> 4);
+                            // term 1: Qhi Klo; term 2: Qlo Khi (A: BF16 pairs, 8 columns per product)
+                            tc::mma_bf16_ts(tmem + scol, tmem + kPColQlo + (term == 2 ? 64 : 0) + 8 * kk,
+                                            bdesc, idesc_s16, 1u);
+                        }
+                    }
+                } else {
+#pragma unroll
+                    for (int term = 0; term < 3; ++term) {
+#pragma unroll
+                        for (int kk = 0; kk < kPHd / 8; ++kk) {
+                            const uint64_t bdesc = dk + (term == 1 ? kLoStep : 0) +
+                                                   uint64_t(((kk >> 2) * (kPKeys * 128) + (kk & 3) * 32) >> 4);
+                            tc::mma_tf32_ts(tmem + scol, tmem + (term == 2 ? kPColQlo : kPColQhi) + 8 * kk,
+                                            bdesc, idesc_s, (term > 0 || kk > 0) ? 1u : 0u);
+                        }
                     }
                 }
                 tc::commit(&bars.s_full[b]);
@@ -382,14 +453,33 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_tc_pipe_kernel(const PAr
             const uint32_t scol = kPColS + 64u * b;
             const uint64_t dv = b ? dvhi[1] : dvhi[0];
             if (leader) {
+                if (BFC) {
 #pragma unroll
-                for (int term = 0; term < 3; ++term) {
-                    if (term == 2) tc::commit(&bars.ph_free[b]);
+                    for (int kk = 0; kk < kPKeys / 8; ++kk)  // Phi Vhi, TF32
+                        tc::mma_tf32_ts(tmem + kPColO, tmem + scol + 8 * kk, dv + uint64_t(kk * 2),
+                                        idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+                    tc::commit(&bars.ph_free[b]);
 #pragma unroll
-                    for (int kk = 0; kk < kPKeys / 8; ++kk) {
-                        const uint64_t bdesc = dv + (term == 1 ? kLoStep : 0) + uint64_t(kk * 2);
-                        tc::mma_tf32_ts(tmem + kPColO, tmem + scol + (term == 2 ? 32 : 0) + 8 * kk,
-                                        bdesc, idesc_o, (j > 0 || term > 0 || kk > 0) ? 1u : 0u);
+                    for (int term = 1; term < 3; ++term) {
+#pragma unroll
+                        for (int kk = 0; kk < kPKeys / 16; ++kk) {
+                            // term 1: Phi (cells +32) . Vlo (bytes 64-127);
+                            // term 2: Plo (cells +48) . Vhi (bytes 0-63)
+                            const uint64_t bdesc = dv + kLoStep + uint64_t(((term == 1 ? 64 : 0) + 32 * kk) >> 4);
+                            tc::mma_bf16_ts(tmem + kPColO, tmem + scol + (term == 1 ? 32 : 48) + 8 * kk,
+                                            bdesc, idesc_o16, 1u);
+                        }
+                    }
+                } else {
+#pragma unroll
+                    for (int term = 0; term < 3; ++term) {
+                        if (term == 2) tc::commit(&bars.ph_free[b]);
+#pragma unroll
+                        for (int kk = 0; kk < kPKeys / 8; ++kk) {
+                            const uint64_t bdesc = dv + (term == 1 ? kLoStep : 0) + uint64_t(kk * 2);
+                            tc::mma_tf32_ts(tmem + kPColO, tmem + scol + (term == 2 ? 32 : 0) + 8 * kk,
+                                            bdesc, idesc_o, (j > 0 || term > 0 || kk > 0) ? 1u : 0u);
+                        }
                     }
                 }
                 tc::commit(&bars.op_empty[b]);
@@ -463,20 +553,20 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_tc_pipe_kernel(const PAr
     if (warp == 0) tc::dealloc(tmem, kPTmemCols);
 }
 
-template <int G>
+template <int G, bool BFC>
 int launch_pipe_g(leap_ctx *c, const PArgs &a) {
-    const void *fn = reinterpret_cast<const void *>(prefill_tc_pipe_kernel<G>);
+    const void *fn = reinterpret_cast<const void *>(prefill_tc_pipe_kernel<G, BFC>);
     if (const int st = set_kernel_smem(fn, kPSmem, "cudaFuncSetAttribute(prefill_tc_pipe)")) return st;
     constexpr int BT = kPRows / G;
     dim3 grid(c->n_kv, (a.n_tok + BT - 1) / BT);
-    prefill_tc_pipe_kernel<G><<<grid, kPThreads, kPSmem, c->stream>>>(a);
+    prefill_tc_pipe_kernel<G, BFC><<<grid, kPThreads, kPSmem, c->stream>>>(a);
     return cuda_status(cudaGetLastError(), "prefill_tc_pipe_kernel launch");
 }
 
 }  // namespace
 
 int launch_prefill_tc_pipe(leap_ctx *c, const float *qrot, const float *kc, const float *vc,
-                           float *out, int pos0, int n_tok) {
+                           float *out, int pos0, int n_tok, bool bf16_corrections) {
     if (c->hd != kPHd) {
         set_error("tensor-core prefill handles head_dim 128");
         return LEAP_ERR_INVALID;
@@ -492,11 +582,15 @@ int launch_prefill_tc_pipe(leap_ctx *c, const float *qrot, const float *kc, cons
     a.n_tok = n_tok;
     a.n_heads = c->n_heads;
     a.scale_log2 = kLog2e / sqrtf(float(kPHd));
-    switch (c->group) {
-        case 1: return launch_pipe_g<1>(c, a);
-        case 2: return launch_pipe_g<2>(c, a);
-        case 4: return launch_pipe_g<4>(c, a);
-        case 8: return launch_pipe_g<8>(c, a);
+    switch (c->group * 2 + (bf16_corrections ? 1 : 0)) {
+        case 2: return launch_pipe_g<1, false>(c, a);
+        case 3: return launch_pipe_g<1, true>(c, a);
+        case 4: return launch_pipe_g<2, false>(c, a);
+        case 5: return launch_pipe_g<2, true>(c, a);
+        case 8: return launch_pipe_g<4, false>(c, a);
+        case 9: return launch_pipe_g<4, true>(c, a);
+        case 16: return launch_pipe_g<8, false>(c, a);
+        case 17: return launch_pipe_g<8, true>(c, a);
         default:
             set_error("unsupported kv_mul %d", c->group);
             return LEAP_ERR_INVALID;

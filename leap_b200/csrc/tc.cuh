@@ -6,6 +6,7 @@
 // 16-byte granule g of row r stored at granule g ^ (r % 8).
 #pragma once
 
+#include <cuda_bf16.h>
 #include <stdint.h>
 
 #include "common.cuh"
@@ -149,6 +150,54 @@ __device__ __forceinline__ void st32(uint32_t taddr, const float (&v)[32]) {
         "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
         "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
         : "memory");
+}
+
+// Thread i of the warp writes 16 consecutive 32-bit columns of TMEM lane
+// (warp's lane base + i), starting at column `taddr & 0xffff`.
+__device__ __forceinline__ void st16u(uint32_t taddr, const uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+        "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
+        "r"(v[15])
+        : "memory");
+}
+
+// 32-bit instruction descriptor for kind::f16 with BF16 A and B (format 1),
+// F32 accumulate, both K-major, dense (the layout of idesc_tf32).
+__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(N >> 3) << 17) |
+           (uint32_t(M >> 4) << 24);
+}
+
+// D[tmem] (+)= A[tmem] . B[smem desc]^T, BF16 operands (K = 16 per product;
+// A in TMEM holds two BF16 values of consecutive k per 32-bit column).
+__device__ __forceinline__ void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                            uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+        :
+        : "r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Two floats rounded to BF16 (nearest even) in one 32-bit word: `a` in the
+// low half (the lower k), `b` in the high half.
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t *>(&v);
+}
+
+// Byte offset of 16-bit element (row, k) in a K-major SW128 operand made of
+// 64-element K chunks of `rows` rows each (chunk = rows*128 bytes).
+__device__ __forceinline__ uint32_t sw128_offset_b16(int row, int k, int rows) {
+    const int chunk = k >> 6;
+    const int gran = (k & 63) >> 3;
+    return uint32_t(chunk * rows * 128 + (row >> 3) * 1024 + (row & 7) * 128 +
+                    ((gran ^ (row & 7)) << 4) + ((k & 7) << 1));
 }
 
 // TF32 split: hi keeps the top 10 explicit mantissa bits (the rest cleared),
