@@ -12,10 +12,12 @@
 //   warps 4-11 (256 threads): convert the FP32 K/V tile j+2 staged by bulk
 //              copies into TF32 hi/lo operand tiles (K-major, 128-byte
 //              swizzle; V transposed);
-//   warp 12    (one elected lane): issue the bulk copies and every tcgen05.mma,
-//              whichever is ready first (S(j+1) = Q K(j+1)^T runs while the
-//              softmax works on S(j); O += P(j) V(j) as soon as P(j) is in
-//              TMEM; a stage's next copy as soon as the converters free it).
+//   warp 12    (one elected lane): issue every tcgen05.mma, whichever is
+//              ready first (S(j+1) = Q K(j+1)^T runs while the softmax works
+//              on S(j); O += P(j) V(j) as soon as P(j) is in TMEM);
+//   warp 13    (one elected lane): a staging buffer's next bulk copies as soon
+//              as the converters free it (apart from the MMA issue, which
+//              blocks while the tensor core's queue is full).
 //
 // Key tiles are 32 keys so that everything can be double-buffered:
 //   TMEM (512 columns): Q hi [0,128) Q lo [128,256) O [256,384)
@@ -47,7 +49,7 @@ constexpr int kPRows = 128;                  // query rows per CTA = TMEM lanes
 constexpr int kPKeys = 32;                   // keys per tile
 constexpr int kPHd = 128;
 constexpr int kPConv = 8;                    // converter warps
-constexpr int kPThreads = 32 * (4 + kPConv + 1);  // softmax, convert, issue warps
+constexpr int kPThreads = 32 * (4 + kPConv + 2);  // softmax, convert, MMA, copy warps
 constexpr uint32_t kPColQhi = 0, kPColQlo = 128, kPColO = 256, kPColS = 384;
 constexpr uint32_t kPTmemCols = 512;
 constexpr float kPMaxLag = 8.0f;
@@ -373,25 +375,38 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_tc_pipe_kernel(const PAr
             }
         }
         if (!ok && lane == 0) atomicExch(&s_fail, 1);
-    } else {  // warp 4 + kPConv
-        // ================= issuer: bulk copies and tensor-core products ========
-        // The whole warp runs the schedule (waits are warp-uniform); one
-        // elected lane issues, with descriptors precomputed per buffer.
+    } else if (warp == 4 + kPConv + 1) {
+        // ================= copy producer: staging buffer j%2 <- tile j =========
+        // Tile j+2 is requested the moment the converters have taken tile j.
         const bool leader = tc::elect_one_sync();
-        auto wait_all = [&](uint64_t *bar, uint32_t parity) {
-            return __all_sync(0xffffffffu, mbar_wait(bar, parity));
-        };
-        auto stage = [&](int j) {
-            const int b = j & 1;
+        bool ok = true;
+        int staged = 0;
+        for (; staged < n_kt; ++staged) {
+            const int j = staged, b = j & 1;
+            if (j >= 2) ok = __all_sync(0xffffffffu, mbar_wait(&bars.st_empty[b], par(j - 2)));
+            if (!ok) break;
             const int k0 = j * kPKeys;
-            const int nr = min(kPKeys, kv_end - k0);
-            const uint32_t bytes = uint32_t(nr) * kPHd * 4;
+            const uint32_t bytes = uint32_t(min(kPKeys, kv_end - k0)) * kPHd * 4;
             if (leader) {
                 mbar_arrive_expect_tx(&bars.st_full[b], 2 * bytes);
                 bulk_g2s(base + kPOffStK(b), gK + size_t(k0) * kPHd, bytes, &bars.st_full[b]);
                 bulk_g2s(base + kPOffStV(b), gV + size_t(k0) * kPHd, bytes, &bars.st_full[b]);
             }
             __syncwarp();
+        }
+        if (!ok && leader) atomicExch(&s_fail, 1);
+        // the last copy into each buffer has landed before shared memory goes
+        for (int b = 0; b < 2; ++b) {
+            const int lt = staged - 1 - ((staged - 1 - b) & 1);
+            if (lt >= 0) (void)mbar_wait(&bars.st_full[b], par(lt));
+        }
+    } else {  // warp 4 + kPConv
+        // ================= MMA issuer ==========================================
+        // The whole warp runs the schedule (waits are warp-uniform); one
+        // elected lane issues, with descriptors precomputed per buffer.
+        const bool leader = tc::elect_one_sync();
+        auto wait_all = [&](uint64_t *bar, uint32_t parity) {
+            return __all_sync(0xffffffffu, mbar_wait(bar, parity));
         };
         const uint32_t idesc_s = tc::idesc_tf32(kPRows, kPKeys);
         const uint32_t idesc_o = tc::idesc_tf32(kPRows, kPHd);
@@ -402,8 +417,7 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_tc_pipe_kernel(const PAr
         const uint64_t dvhi[2] = {tc::sw128_kmajor_desc(sbase + kPOffVThi(0)),
                                   tc::sw128_kmajor_desc(sbase + kPOffVThi(1))};
         constexpr uint64_t kLoStep = kPOpBytes >> 4;  // hi -> lo tile of the same buffer
-        int staged = 0, s_issued = 0, pv_issued = 0;
-        for (; staged < min(2, n_kt); ++staged) stage(staged);
+        int s_issued = 0, pv_issued = 0;
         bool ok = wait_all(&bars.q_ready, 0);
         auto issue_s = [&](int j) {  // S(j) = Qhi Khi + Qhi Klo + Qlo Khi  (M 128, N 32, K 128)
             const int b = j & 1;
@@ -488,11 +502,10 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_tc_pipe_kernel(const PAr
         };
         // Issue whichever step is ready: S(j) once tile j's K operands are
         // converted and PV(j-2)'s P-hi terms have released buffer j%2's S
-        // columns; PV(j) once the
-        // softmax has written P(j) and tile j's V operands are converted; the
-        // copy of tile j+2 once the converters have taken tile j from staging.  Every test is of the next phase of
-        // its barrier only (the one before it was observed), so parities
-        // cannot alias.  No progress for kMaxWaitNs ends the loop.
+        // columns; PV(j) once the softmax has written P(j) and tile j's V
+        // operands are converted.  Every test is of the next phase of its
+        // barrier only (the one before it was observed), so parities cannot
+        // alias.  No progress for kMaxWaitNs ends the loop.
         unsigned long long t_idle = global_ns();
         uint32_t idle_polls = 0;
         while (ok && pv_issued < n_kt) {
@@ -518,14 +531,6 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_tc_pipe_kernel(const PAr
                     progress = true;
                 }
             }
-            if (staged < n_kt) {
-                const int j = staged;
-                if (__all_sync(0xffffffffu, mbar_test(&bars.st_empty[j & 1], par(j - 2)))) {
-                    stage(j);
-                    ++staged;
-                    progress = true;
-                }
-            }
             if (progress) {
                 idle_polls = 0;
             } else if ((++idle_polls & 255) == 0) {
@@ -543,8 +548,6 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_tc_pipe_kernel(const PAr
             const int lp = pv_issued - 1 - ((pv_issued - 1 - b) & 1);    // last PV on b
             if (lp >= 0) (void)mbar_wait(&bars.ph_free[b], par(lp));
             if (lp >= 0) (void)mbar_wait(&bars.op_empty[b], par(lp));
-            const int lt = staged - 1 - ((staged - 1 - b) & 1);          // last copy into b
-            if (lt >= 0) (void)mbar_wait(&bars.st_full[b], par(lt));
         }
     }
     tc::fence_before_sync();

@@ -9,8 +9,8 @@ barrier (parities would alias), and every buffer is read only after it was
 written for that item and rewritten only after its readers are done.
 
   prefill_tc_pipe.cu  softmax warps / converter warps (K and V operands of a
-                      tile in two steps) / one issuing lane; the issuer takes
-                      whichever of S(j), PV(j), copy(j) is ready; PV(j) is
+                      tile in two steps) / an MMA-issuing lane taking whichever
+                      of S(j), PV(j) is ready / a copy warp; PV(j) is
                       its P-hi products then its P-lo products, with a commit
                       between them; MMAs complete in issue order.
   engine_kernels.cu   gemv_q8_stream_kernel: dot warps / copy producer /
