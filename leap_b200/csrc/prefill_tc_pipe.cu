@@ -221,17 +221,24 @@ __global__ void __launch_bounds__(kPThreads, 1) prefill_tc_pipe_kernel(const PAr
             if (move) m = mt;
             // Key 0 is in every row's first tile, so m is finite from here
             // on and a masked score gives exp2(-inf) = +0.
-            const float neg_m = -m;
-            float rsp[4] = {0.f, 0.f, 0.f, 0.f};
+            // Key pairs in packed FP32x2 instructions (each half rounded as
+            // the scalar fma / add); the four sum chains are the pairs' halves.
+            const float2 scl2 = make_float2(a.scale_log2, a.scale_log2);
+            const float2 nm2 = make_float2(-m, -m);
+            float2 rsp[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
             float phi[32], plo[32];
 #pragma unroll
-            for (int c = 0; c < 32; ++c) {
-                const float p = fast_exp2(fmaf(s[c], a.scale_log2, neg_m));
-                rsp[c & 3] += p;
-                phi[c] = tc::tf32_hi(p);
-                plo[c] = p - phi[c];
+            for (int c2 = 0; c2 < 16; ++c2) {
+                const float2 e = __ffma2_rn(make_float2(s[2 * c2], s[2 * c2 + 1]), scl2, nm2);
+                const float2 p = make_float2(fast_exp2(e.x), fast_exp2(e.y));
+                rsp[c2 & 1] = __fadd2_rn(rsp[c2 & 1], p);
+                phi[2 * c2] = tc::tf32_hi(p.x);
+                phi[2 * c2 + 1] = tc::tf32_hi(p.y);
+                const float2 lo = __fadd2_rn(p, make_float2(-phi[2 * c2], -phi[2 * c2 + 1]));
+                plo[2 * c2] = lo.x;
+                plo[2 * c2 + 1] = lo.y;
             }
-            l = l * alpha + ((rsp[0] + rsp[1]) + (rsp[2] + rsp[3]));
+            l = l * alpha + ((rsp[0].x + rsp[0].y) + (rsp[1].x + rsp[1].y));
             tc::st32(tmem + lane_off + scol, phi);
             if (BFC) {
                 float p16[32];  // BF16 pairs: P hi in cells 0-15, P lo in 16-31
