@@ -72,6 +72,19 @@ def test_null_context_is_an_error():
         _native.check(lib.leap_kv_clear(None))
 
 
+def test_kernel_selectors_validate_their_argument():
+    """The process-wide W8A8 kernel selectors take only the kernels they
+    name, and report the choices in the message; valid choices need no GPU."""
+    lib = _native.lib()
+    assert lib.leap_op_set_q8_gemm(2) == _native.LEAP_ERR_INVALID
+    assert b"kind::i8" in lib.leap_last_error()
+    assert lib.leap_op_set_q8_gemv(3) == _native.LEAP_ERR_INVALID
+    assert lib.leap_op_set_q8_gemm(0) == _native.LEAP_OK
+    assert lib.leap_op_set_q8_gemm(1) == _native.LEAP_OK  # the library default
+    assert lib.leap_op_set_q8_gemv(2) == _native.LEAP_OK  # the library default
+    assert lib.leap_set_prefill_impl(None, 3) == _native.LEAP_ERR_INVALID  # needs a context
+
+
 def test_no_gpu_fails_loudly():
     """Without a GPU the context cannot be created, and says why; there is
     no CPU fallback."""
